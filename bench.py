@@ -1,0 +1,461 @@
+"""Benchmark of the skinny-GEMM hot path on B200.
+
+Default (the driver's line): BASELINE config 1, the fp16 skinny GEMM at lm_head shape
+M=7, K=5120, N=151936 (1.56 GB of weights, larger than the 126 MB L2, so no flush is needed).
+One step = one GEMM through the C ABI on device-resident operands. With N GPUs (torchrun, one
+rank per GPU) every rank runs its own config-1 GEMM (weak scaling; column-parallel shards need no
+collective); `value` is the aggregate HBM throughput of all ranks, timed as the max over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+    python bench.py --impl reference      # the reference's CPU path (torch dequant+matmul)
+    python bench.py --sweep               # every BASELINE config, one JSON line each (not timed by the driver)
+
+Metric: HBM TB/s of algorithmic bytes (2*N*K + 2*M*K + 2*M*N for fp16; the W4 formula for W4),
+and us per GEMM.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "W4A16/fp16 skinny-GEMM HBM throughput at M<=8 (config 1: fp16 lm_head GEMM)"
+UNIT = "TB/s"
+CFG1 = dict(M=7, K=5120, N=151936)
+FALLBACK_HBM_GBS = 6650.0
+
+
+def f16_bytes(M, K, N):
+    return 2 * N * K + 2 * M * K + 2 * M * N
+
+
+def w4_bytes(M, K, N, G):
+    return K * N // 2 + (K // G) * N * 2 + (K // G) * N // 2 + 2 * M * K + 2 * M * N
+
+
+def hbm_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def recorded_traffic(kernel: str, workload: str):
+    """DRAM bytes per launch of `kernel` on `workload` from a committed ncu summary, or None."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get(kernel, {}).get(workload)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while the timed region runs."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int, period_s: float = 0.01):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+        self.period = period_s
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------------
+# distributed plumbing
+# ------------------------------------------------------------------------------------------------
+
+
+def dist_setup(n_gpus: int):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    if world != n_gpus and not (world == 1 and n_gpus == 1):
+        print(f"warning: --gpus {n_gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    return rank, world, local
+
+
+def barrier_sync(world):
+    import torch
+
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU baseline: the reference's own torch path (kernels/bench_skinny.py:44; kernels/check_w4.py)
+# ------------------------------------------------------------------------------------------------
+
+
+def cpu_baseline_f16(x_cpu, w_rows_cpu, budget_s: float = 10.0):
+    """Time `x.float() @ w.float().T` (the reference's fp16 GEMM reference) on the host cores
+    over a row sample of the weights; returns (TB/s, seconds per call, cores, description)."""
+    import torch
+
+    from oracle import cpu_baseline
+
+    return cpu_baseline.time_f16(x_cpu, w_rows_cpu, budget_s=budget_s)
+
+
+# ------------------------------------------------------------------------------------------------
+# GPU legs
+# ------------------------------------------------------------------------------------------------
+
+
+def time_steps(fn, steps: int, world: int, stream):
+    """Time exactly `steps` calls of fn between barriers; per-step CUDA events on `stream`."""
+    import torch
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier_sync(world)
+    start.record(stream)
+    for s, e in evs:
+        s.record(stream)
+        fn()
+        e.record(stream)
+    end.record(stream)
+    barrier_sync(world)
+    total_ms = start.elapsed_time(end)
+    per = [s.elapsed_time(e) for s, e in evs]
+    return total_ms, per
+
+
+def run_gpu(args):
+    import torch
+
+    import __graft_entry__ as entry
+
+    rank, world, local = dist_setup(args.gpus)
+    pkg = entry.load_package()
+    from mi50_vllm_lab_b200 import capi
+
+    ops = pkg.ops()
+    lib = capi.lib()
+    M, K, N = CFG1["M"], CFG1["K"], CFG1["N"]
+    nbytes = f16_bytes(M, K, N)
+
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    ws = torch.zeros(lib.b2_workspace_bytes(local), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        rc = lib.b2_gemm_f16(x.data_ptr(), w.data_ptr(), y.data_ptr(), M, K, N, ws.data_ptr(),
+                             ws.numel(), sp)
+        if rc:
+            capi.check(rc, "b2_gemm_f16")
+
+    for _ in range(args.warmup):
+        step()
+    with ClockSampler(local) as clk:
+        total_ms, per = time_steps(step, args.steps, world, stream)
+    ms_step = max_over_ranks(total_ms / args.steps, world)
+    kern_ms = sum(per) / len(per)
+    value = world * nbytes / (ms_step * 1e-3) / 1e12
+
+    # end to end through the plugin API with host buffers: H2D of the activations, the GEMM,
+    # D2H of the logits, every step
+    x_host = torch.randn(M, K, generator=torch.Generator().manual_seed(7)).half().pin_memory()
+    y_host = torch.empty(M, N, dtype=torch.float16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        out = ops.gemm(x_dev, w, 20)
+        y_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    e2e_ms, _ = time_steps(e2e_step, args.steps, world, stream)
+    e2e_step_ms = max_over_ranks(e2e_ms / args.steps, world)
+    e2e_value = world * nbytes / (e2e_step_ms * 1e-3) / 1e12
+
+    peak, peak_kind = hbm_peak()
+    achieved = nbytes / (kern_ms * 1e-3) / 1e9
+    clocks = clk.summary()
+    status = ops.workspace_status(False)
+    assert status == 0, f"device status {status}"
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+            "us_per_gemm": round(ms_step * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 (fp32 accumulate)", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+            "config": {"workload": "config 1: fp16 skinny GEMM, lm_head shape", "M": M, "K": K,
+                       "N": N, "per_gpu_bytes_per_step": nbytes,
+                       "l2": "weights 1.56 GB > 126 MB L2 (no flush needed)",
+                       "parallelism": f"{world} independent column shards (no collective)"},
+            "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "ms_per_step": round(e2e_step_ms, 5),
+                    "api": "torch.ops.gfx906_skinny.gemm, pinned host x -> device, y -> pinned host",
+                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                         "kernel": "gemm_f16_kernel", "kernel_us": round(kern_ms * 1e3, 2),
+                         "traffic": recorded_traffic("gemm_f16_kernel", "config1")},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        rows = 8192
+        cpu = cpu_baseline_f16(x.cpu(), w[:rows].cpu(), budget_s=args.cpu_seconds)
+        line["cpu_baseline"] = cpu
+    if line:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference's CPU implementation of the path (oracle port of kernels/bench_skinny.py:44:
+    `x.float() @ w.float().T`), on the same config and metric, all host threads."""
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import cpu_baseline
+
+    M, K, N = CFG1["M"], CFG1["K"], CFG1["N"]
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(1234)
+    x = torch.randn(M, K, generator=g).half()
+    w = (torch.randn(8192, K, generator=g) * 0.02).half()
+    # size the per-step sample so that warm-up + steps stay within about two minutes
+    t0 = time.perf_counter()
+    cpu_baseline.f16_reference(x, w)
+    t_full = time.perf_counter() - t0
+    per_step = 120.0 / (args.steps + args.warmup)
+    rows = int(max(256, min(8192, 8192 * per_step / max(t_full, 1e-6))) // 256 * 256)
+    w = w[:rows].contiguous()
+    step = lambda: cpu_baseline.f16_reference(x, w)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    sample_bytes = f16_bytes(M, K, rows)
+    value = sample_bytes / sec / 1e12
+    desc = (f"{rows} of {N} weight rows per step ({sample_bytes / f16_bytes(M, K, N):.3f} of a "
+            f"config-1 GEMM); torch {torch.__version__} float32 matmul")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT,
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+        "ms_per_full_gemm": round(sec * 1e3 * N / rows, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32 (reference computes x.float() @ w.float().T)", "data": "synthetic",
+        "config": {"workload": "config 1: fp16 skinny GEMM, lm_head shape", "M": M, "K": K,
+                   "N": N, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_sweep(args):
+    from oracle import cpu_baseline  # noqa: F401  (imported for symmetry; sweep is GPU-only)
+
+    import torch
+
+    import __graft_entry__ as entry
+
+    pkg = entry.load_package()
+    from mi50_vllm_lab_b200 import capi
+
+    lib = capi.lib()
+    torch.cuda.set_device(0)
+    ws = torch.zeros(lib.b2_workspace_bytes(0), dtype=torch.uint8, device="cuda")
+    sp = torch.cuda.current_stream().cuda_stream
+    stream = torch.cuda.current_stream()
+    peak, _ = hbm_peak()
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+
+    def bench_w4(name, M, K, N, G):
+        nb = w4_bytes(M, K, N, G)
+        copies = max(1, int(3 * l2 // (K * N // 2)) + 1)
+        g = torch.Generator(device="cuda").manual_seed(M * K + N)
+        sets = []
+        for _ in range(copies):
+            qw = torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32, generator=g)
+            qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda", dtype=torch.int32, generator=g)
+            sc = (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half()
+            sets.append((qw, qz, sc))
+        x = torch.randn(M, K, device="cuda", generator=g).half()
+        y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        it = [0]
+
+        def step():
+            qw, qz, sc = sets[it[0] % copies]
+            it[0] += 1
+            capi.check(lib.b2_w4_gemm(x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(),
+                                      y.data_ptr(), M, K, N, G, ws.data_ptr(), ws.numel(), sp))
+        for _ in range(max(args.warmup, copies)):
+            step()
+        _, per = time_steps(step, args.steps, 1, stream)
+        us = statistics.median(per) * 1e3
+        return {"workload": name, "M": M, "K": K, "N": N, "G": G, "us": round(us, 2),
+                "TBps": round(nb / us / 1e6, 3), "frac": round(nb / us / 1e3 / peak, 3),
+                "l2_rotation_copies": copies}
+
+    def bench_f16(name, M, K, N):
+        nb = f16_bytes(M, K, N)
+        copies = max(1, int(3 * l2 // (2 * N * K)) + 1)
+        g = torch.Generator(device="cuda").manual_seed(N)
+        ws_ = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).half() for _ in range(copies)]
+        x = torch.randn(M, K, device="cuda", generator=g).half()
+        y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        it = [0]
+
+        def step():
+            w = ws_[it[0] % copies]
+            it[0] += 1
+            capi.check(lib.b2_gemm_f16(x.data_ptr(), w.data_ptr(), y.data_ptr(), M, K, N,
+                                       ws.data_ptr(), ws.numel(), sp))
+        for _ in range(max(args.warmup, copies)):
+            step()
+        _, per = time_steps(step, args.steps, 1, stream)
+        us = statistics.median(per) * 1e3
+        return {"workload": name, "M": M, "K": K, "N": N, "us": round(us, 2),
+                "TBps": round(nb / us / 1e6, 3), "frac": round(nb / us / 1e3 / peak, 3),
+                "l2_rotation_copies": copies}
+
+    rows = [bench_f16("cfg1 lm_head", 7, 5120, 151936), bench_w4("cfg0", 7, 4096, 4096, 128)]
+    for M in (1, 2, 4, 8):
+        for nm, (K, N) in {"qkv": (5120, 8192), "o_proj": (6144, 5120), "gate_up": (5120, 34816),
+                           "down": (17408, 5120)}.items():
+            rows.append(bench_w4(f"cfg2 {nm}", M, K, N, 128))
+    for P in (2, 4, 8):
+        rows.append(bench_w4(f"cfg3 down shard TP{P}", 8, 17408 // P, 5120, 128))
+    for M in (1, 8):
+        rows.append(bench_f16("drafter fc", M, 25600, 5120))
+    for r in rows:
+        print(json.dumps(r), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    elif args.sweep:
+        if args.steps > 500:
+            args.steps = 200
+        run_sweep(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,178 @@
+/*
+ * b2_skinny.h - C ABI of the B200 (sm_100a) skinny-GEMM library.
+ *
+ * Speculative decoding verifies k+1 <= 8 tokens per step, so the projections of a
+ * verify step are GEMMs with M <= 8 activation rows. They are bound by HBM bandwidth.
+ * This library provides, behind plain pointers and sizes:
+ *   - an fp16 GEMM        y[M,N] = x[M,K] @ w[N,K]^T                      (b2_gemm_f16)
+ *   - a W4A16 GEMM over GPTQ/Exllama-shuffled 4-bit weights                (b2_w4_gemm)
+ *   - a one-shot all-reduce over NVLink peer memory                        (b2_nvar_*)
+ *   - the W4A16 GEMM with that all-reduce fused into its epilogue          (b2_w4_gemm_allreduce)
+ * Every compute entry point launches on the caller's stream, never synchronises and never
+ * allocates, so it can be captured in a CUDA graph.
+ *
+ * Conventions
+ *   - Pointers to device memory are plain `void*`; `stream` is a cudaStream_t (0 = legacy
+ *     default stream).
+ *   - Every entry point returns a b2 status code (B2_OK == 0). b2_last_error() gives a
+ *     one-line detail of the last failure on the calling thread.
+ *   - fp16 means IEEE binary16; int4 weights are packed 8 per 32-bit word.
+ *
+ * Reference interfaces (paths inside the reference project 0c33/mi50-vllm-lab):
+ *   kernels/skinny.cu:300-333   gemm(Tensor x, Tensor w, int variant=0) -> Tensor
+ *   kernels/w4.cu:477-509       w4gemm(Tensor a, Tensor qw, Tensor qz, Tensor sc, int kw, int waves)
+ *   kernels/hostar.cu:114-166   hostar_create / hostar_unlink / hostar_max_bytes / hostar_allreduce
+ */
+#ifndef B2_SKINNY_H
+#define B2_SKINNY_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2_ABI_VERSION 1
+
+/* ------------------------------------------------------------------------------------------
+ * Status codes
+ * ---------------------------------------------------------------------------------------- */
+#define B2_OK 0
+#define B2_ERR_INVALID_ARG 1 /* shape, dtype, alignment or pointer outside the contract      */
+#define B2_ERR_UNSUPPORTED 2 /* the device is not an sm_100 part, or a needed feature is off */
+#define B2_ERR_CUDA 3        /* a CUDA runtime or driver call failed (detail in last_error)  */
+#define B2_ERR_WORKSPACE 4   /* workspace missing or smaller than b2_workspace_bytes()       */
+#define B2_ERR_TIMEOUT 5     /* a bounded device-side wait gave up (peer never arrived)      */
+#define B2_ERR_STATE 6       /* bad handle, or an all-reduce handle that is not connected    */
+
+/* Element types for the all-reduce. */
+#define B2_DTYPE_F16 0
+#define B2_DTYPE_F32 1
+
+/* Short text for a status code (static storage). */
+const char* b2_status_string(int status);
+/* Detail of the last failure on this thread (thread-local storage, "" when none). */
+const char* b2_last_error(void);
+/* B2_ABI_VERSION of the loaded library. */
+int b2_abi_version(void);
+
+/* ------------------------------------------------------------------------------------------
+ * Workspace
+ *
+ * The GEMMs split K across CTAs (stream-K). Partial sums go to fp32 slots in a workspace and
+ * the last CTA to finish a tile adds them in a fixed order, so results are deterministic.
+ * The workspace also holds one self-resetting arrival counter per output tile and a status
+ * word. It must be zero-filled once (b2_workspace_init) before its first use; every call
+ * leaves the counters at zero again. Calls that share a workspace must not overlap on the
+ * GPU (issue them on one stream). Replaces the per-call at::empty split-K buffer of
+ * kernels/w4.cu:330-334 and the separate w4_reduce_kernel launch (kernels/w4.cu:154-166).
+ * ---------------------------------------------------------------------------------------- */
+
+/* Bytes of workspace that cover every supported shape on `device` (fixed per device). */
+size_t b2_workspace_bytes(int device);
+/* Zero-fill a workspace on `stream` (asynchronous). */
+int b2_workspace_init(void* ws, size_t ws_bytes, void* stream);
+/* Synchronously read the workspace status word: 0, or the B2_ERR_* code a kernel recorded
+ * when one of its bounded waits gave up. Clears the word when `clear` is non-zero. */
+int b2_workspace_status(void* ws, int clear, int* device_status);
+
+/* ------------------------------------------------------------------------------------------
+ * fp16 skinny GEMM          y[M,N] = x[M,K] @ w[N,K]^T, fp32 accumulation, fp16 output
+ *
+ * Replaces skinny_gemm (kernels/skinny.cu:300-328, op `gemm`, schema at :331).
+ *   x : [M, K] fp16, row-major, 16-byte aligned          1 <= M <= 8
+ *   w : [N, K] fp16, row-major (K contiguous), 16-byte aligned, K % 8 == 0
+ *   y : [M, N] fp16, row-major (written)
+ * ---------------------------------------------------------------------------------------- */
+int b2_gemm_f16(const void* x, const void* w, void* y, int M, int K, int N, void* ws,
+                size_t ws_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * W4A16 skinny GEMM         y[M,N] = a[M,K] @ dequant(qw, qz, sc)[K,N]
+ *
+ * Replaces w4_gemm (kernels/w4.cu:479-504, op `w4gemm`, schema at :507). Same layouts as the
+ * reference (kernels/w4.cu:477-478, kernels/check_w4.py:11-18):
+ *   a  : [M, K] fp16 row-major                                         1 <= M <= 8
+ *   qw : [K/8, N] int32. Word (r, n) holds k = 8r..8r+7 of column n: nibble i (bits 4i..4i+3)
+ *        is k = 8r+2i and nibble 4+i (bits 16+4i..) is k = 8r+2i+1, for i = 0..3.
+ *   qz : [K/G, N/8] int32. Nibble c of word (g, j) is the zero point of column 8j+c ("v2"
+ *        format: no +1 offset).
+ *   sc : [K/G, N] fp16 scales.
+ *   w[k][n] = (q[k][n] - z[k/G][n]) * sc[k/G][n]; fp32 accumulation; fp16 output.
+ * Contract: K % 128 == 0, N % 32 == 0, G in {32, 64} or G a multiple of 128, K % G == 0,
+ * all pointers 16-byte aligned.
+ * ---------------------------------------------------------------------------------------- */
+int b2_w4_gemm(const void* a, const void* qw, const void* qz, const void* sc, void* y, int M,
+               int K, int N, int group_size, void* ws, size_t ws_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
+ * Host-side rendezvous registry (POSIX shared memory, no GPU needed)
+ *
+ * Ranks of one node publish fixed-size blobs (CUDA IPC handles) under a shared-memory name and
+ * read each other's. Generalises the shm_open/mmap set-up of hostar_create
+ * (kernels/hostar.cu:114-134) from two ranks to `world` ranks.
+ * ---------------------------------------------------------------------------------------- */
+#define B2_BLOB_BYTES 64
+typedef struct b2_registry b2_registry;
+int b2_registry_open(const char* name, int world, int create, b2_registry** out);
+int b2_registry_put(b2_registry* reg, int rank, const void* blob);
+/* B2_ERR_STATE when `rank` has not published yet. */
+int b2_registry_get(b2_registry* reg, int rank, void* blob_out);
+int b2_registry_close(b2_registry* reg);
+/* Replaces hostar_unlink (kernels/hostar.cu:136). */
+int b2_registry_unlink(const char* name);
+
+/* ------------------------------------------------------------------------------------------
+ * NVLink one-shot all-reduce (replaces the host-memory all-reduce of kernels/hostar.cu)
+ *
+ * Each rank owns a device buffer: a generation counter, per-rank flags and two
+ * parity-alternating sets of `world` data slots. A call pushes this rank's data into its slot
+ * on every peer over NVLink, publishes a flag with release semantics, waits (bounded) for all
+ * peers' flags and sums the `world` slots in rank order 0..world-1 in fp32. Every rank
+ * therefore computes bit-identical results. The generation lives on the device, so calls can
+ * be replayed from a CUDA graph (same protocol as kernels/hostar.cu:9-14, generalised to
+ * `world` ranks). No TMA, no multicast.
+ * ---------------------------------------------------------------------------------------- */
+typedef struct b2_nvar b2_nvar;
+#define B2_IPC_HANDLE_BYTES 64
+/* Allocate this rank's buffer on `device` (`slot_bytes` = largest payload per call). */
+int b2_nvar_create(int device, int rank, int world, size_t slot_bytes, b2_nvar** out);
+/* Write this rank's CUDA IPC handle (B2_IPC_HANDLE_BYTES). */
+int b2_nvar_export(const b2_nvar* ar, void* handle_out);
+/* Map the peers' buffers; `handles` holds world * B2_IPC_HANDLE_BYTES in rank order. */
+int b2_nvar_connect(b2_nvar* ar, const void* handles);
+int b2_nvar_is_connected(const b2_nvar* ar);
+/* Largest payload in bytes per call (replaces hostar_max_bytes, kernels/hostar.cu:138). */
+size_t b2_nvar_max_bytes(const b2_nvar* ar);
+/* Bound on each device-side wait for a peer, in nanoseconds (default 10 s). */
+int b2_nvar_set_timeout_ns(b2_nvar* ar, uint64_t ns);
+/* out = sum over ranks of in; `count` elements of `dtype`; count * size % 16 == 0.
+ * Replaces hostar_allreduce (kernels/hostar.cu:140-153). `in` and `out` may alias. */
+int b2_nvar_allreduce(b2_nvar* ar, const void* in, void* out, size_t count, int dtype,
+                      void* stream);
+/* Row-parallel W4A16 layer: y = allreduce_over_ranks(a_rank @ dequant(qw_rank, ...)), with the
+ * all-reduce fused into the GEMM epilogue. Each rank passes its K-shard; M, N, G match on all
+ * ranks. fp32 partials cross NVLink; the fp16 result is bit-identical on every rank. */
+int b2_w4_gemm_allreduce(b2_nvar* ar, const void* a, const void* qw, const void* qz,
+                         const void* sc, void* y, int M, int K, int N, int group_size, void* ws,
+                         size_t ws_bytes, void* stream);
+/* Synchronously read the device error word of the handle (0 or B2_ERR_TIMEOUT). */
+int b2_nvar_status(b2_nvar* ar, int clear, int* device_status);
+int b2_nvar_rank(const b2_nvar* ar);
+int b2_nvar_world(const b2_nvar* ar);
+int b2_nvar_destroy(b2_nvar* ar);
+
+/* ------------------------------------------------------------------------------------------
+ * Tuning (process-wide; for measurement sweeps)
+ * ---------------------------------------------------------------------------------------- */
+#define B2_TUNE_CTAS_PER_SM 1     /* resident CTAs per SM the stream-K grid targets (0 = auto) */
+#define B2_TUNE_MIN_UNITS 2       /* fewest k-units per CTA before the grid shrinks (0 = auto)  */
+int b2_set_tuning(int key, int value);
+int b2_get_tuning(int key);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2_SKINNY_H */

@@ -1,0 +1,172 @@
+// Device-side building blocks shared by the kernels: mbarrier pipeline, TMA, mma.sync,
+// bounded waits, release/acquire flags and the stream-K work split.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b2_skinny.h"
+
+namespace b2 {
+
+// Output tile width (columns of y) of both GEMMs and the M-rows capacity of a slot.
+constexpr int kTileN = 128;
+constexpr int kMaxM = 8;
+constexpr int kSlotFloats = kMaxM * kTileN;  // one fp32 partial tile
+constexpr int kStatusWords = 64;             // status region of the workspace (256 B)
+
+// A device wait that has not finished after this long records B2_ERR_TIMEOUT and returns.
+constexpr unsigned long long kPipeWaitNs = 2000000000ull;  // 2 s (data from HBM: microseconds)
+constexpr unsigned int kMaxSpin = 1u << 30;                // iteration cap on top of the clock
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete. Gives up after kPipeWaitNs, or at once when
+// another warp of the CTA already gave up (*abort != 0); then sets *abort and returns false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (unsigned int it = 1; it < kMaxSpin; ++it) {
+    if (mbar_test(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kPipeWaitNs) break;
+    }
+  }
+  *abort = 1;
+  return false;
+}
+
+// ---------------------------------------------------------------------------------------------
+// TMA (cp.async.bulk.tensor, no multicast) and L2 policy
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// 2-D tiled load of the box at (c0 = innermost coordinate, c1) into shared memory, completing
+// transaction bytes on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0,
+                                            int c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(m), "r"(c0), "r"(c1), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Loads, stores, barriers
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint4 ldg_nc128(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+// Named barrier over the first `threads` threads of the CTA (the consumer warps).
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// System-scope release store / acquire load of a 32-bit flag (peer memory over NVLink).
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Tensor cores: D = A(16x16 f16, row) * B(16x8 f16, col) + C, fp32 accumulate.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---------------------------------------------------------------------------------------------
+// Stream-K work split. The GEMM is cut into `tiles` output tiles of kTileN columns, each made
+// of `upt` k-units. The total tiles*upt units are dealt to `ctas` CTAs as contiguous ranges:
+// CTA i owns units [total*i/ctas, total*(i+1)/ctas). A tile touched by one CTA is written
+// directly; a tile shared by several CTAs is summed by the last of them to finish, in CTA
+// order, from fp32 slots (slot 0 = the CTA's first tile, slot 1 = its last tile).
+// ---------------------------------------------------------------------------------------------
+struct StreamK {
+  long long total;  // tiles * upt
+  int upt;          // k-units per tile
+  int tiles;
+  int ctas;         // grid size; ctas <= total so every CTA owns at least one unit
+};
+
+__host__ __device__ __forceinline__ long long sk_begin(const StreamK& s, int cta) {
+  return s.total * (long long)cta / s.ctas;
+}
+// The CTA whose range contains unit u.
+__host__ __device__ __forceinline__ int sk_owner(const StreamK& s, long long u) {
+  return (int)(((u + 1) * (long long)s.ctas - 1) / s.total);
+}
+// Slot index (0 or 1) that CTA `cta` uses for its partial of tile `tile`.
+__host__ __device__ __forceinline__ int sk_slot(const StreamK& s, int cta, int tile) {
+  return (sk_begin(s, cta) / s.upt == tile) ? 0 : 1;
+}
+
+}  // namespace b2

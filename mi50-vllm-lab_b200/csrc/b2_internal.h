@@ -1,0 +1,53 @@
+// Host-side helpers shared by the translation units of the library (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "b2_skinny.h"
+
+namespace b2 {
+
+// Record a failure detail for b2_last_error() and return `status`.
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+// Check a CUDA runtime call; on error record it and return B2_ERR_CUDA.
+#define B2_CUDA_TRY(expr)                                                             \
+  do {                                                                                \
+    cudaError_t e_ = (expr);                                                          \
+    if (e_ != cudaSuccess)                                                            \
+      return ::b2::fail(B2_ERR_CUDA, "%s failed: %s", #expr, cudaGetErrorString(e_)); \
+  } while (0)
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int major = 0, minor = 0;
+  size_t smem_optin = 0;
+  bool ok = false;
+};
+// Cached properties of the current device (B2_ERR_UNSUPPORTED unless compute capability 10.x).
+int device_info(DeviceInfo* out);
+
+// Encode a 2-D tiled tensor map. dims/box: {inner, outer}; row_stride in bytes.
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+              uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swizzle);
+
+// Workspace layout: [status words][tile counters][partial slots].
+constexpr size_t kWsStatusBytes = 256;
+constexpr int kWsMaxTiles = 65536;
+constexpr int kWsMaxCtas = 1024;
+size_t ws_counters_offset();
+size_t ws_partials_offset();
+size_t ws_total_bytes();
+
+// Tuning knobs (b2_set_tuning).
+int tuning(int key);
+
+// Grid size of a stream-K launch over `total` units for a kernel with `occ` resident CTAs per SM.
+int streamk_ctas(long long total, int sm_count, int occ, int min_units_default);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace b2

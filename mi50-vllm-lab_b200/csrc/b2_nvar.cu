@@ -1,0 +1,285 @@
+// One-shot all-reduce over NVLink peer memory for tensor-parallel ranks of one node.
+//
+// Replaces the two-GPU host-memory all-reduce of kernels/hostar.cu (hostar_create,
+// hostar_allreduce, hostar_kernel). Where the reference writes each rank's slice into pinned host
+// memory over PCIe and spins on a flag in host memory, here every rank stores its data straight
+// into the peers' HBM over NVLink (CUDA IPC mappings), publishes a per-chunk flag with a
+// system-scope release store, and reads the other ranks' data from its own HBM. The protocol
+// (device generation counter, parity-alternating slots, fixed summation order) is described in
+// b2_nvar.cuh. Waits are bounded and never trap: a peer that does not arrive within the handle's
+// timeout leaves B2_ERR_TIMEOUT in the buffer header, which b2_nvar_status() reports.
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+
+#include "b2_device.cuh"
+#include "b2_internal.h"
+#include "b2_nvar.cuh"
+
+struct b2_nvar {
+  int device;
+  int rank;
+  int world;
+  size_t slot_bytes;
+  size_t bytes;
+  char* local;
+  char* peers[b2::kArMaxWorld];
+  bool opened[b2::kArMaxWorld];
+  bool connected;
+  unsigned long long timeout_ns;
+};
+
+namespace b2 {
+namespace {
+
+constexpr int kThreads = 512;
+constexpr size_t kMinChunk = (size_t)kThreads * 16;  // one 16-byte vector per thread
+
+__device__ __forceinline__ void add_vec(float (&acc)[8], const uint4& v, bool is_half) {
+  if (is_half) {
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __half22float2(h[i]);
+      acc[2 * i] += f.x;
+      acc[2 * i + 1] += f.y;
+    }
+  } else {
+    const float* f = reinterpret_cast<const float*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] += f[i];
+  }
+}
+
+__device__ __forceinline__ uint4 pack_vec(const float (&acc)[8], bool is_half) {
+  uint4 r;
+  if (is_half) {
+    __half2* h = reinterpret_cast<__half2*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
+  } else {
+    float* f = reinterpret_cast<float*>(&r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) f[i] = acc[i];
+  }
+  return r;
+}
+
+// CTA c owns bytes [c*chunk, (c+1)*chunk) of the payload and flag index c.
+__global__ void __launch_bounds__(kThreads) nvar_kernel(const uint4* in, uint4* out, size_t nvec,
+                                                        size_t chunk_vec, int is_half,
+                                                        const ArView v) {
+  __shared__ uint32_t s_gen;
+  if (threadIdx.x == 0) s_gen = ar_begin(v);
+  __syncthreads();
+  const uint32_t e = s_gen;
+  const int par = (int)(e & 1u);
+  const size_t lo = (size_t)blockIdx.x * chunk_vec;
+  const size_t hi = (lo + chunk_vec < nvec) ? lo + chunk_vec : nvec;
+
+  // 1. push this rank's chunk into slot[par][rank] of every rank
+  for (size_t i = lo + threadIdx.x; i < hi; i += kThreads) {
+    const uint4 val = in[i];
+    for (int r = 0; r < v.world; ++r)
+      reinterpret_cast<uint4*>(ar_slot(v, r, par, v.rank))[i] = val;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ar_publish(v, blockIdx.x, e);
+    ar_wait(v, blockIdx.x, e);
+  }
+  __syncthreads();
+  __threadfence();
+
+  // 2. add the `world` slots in rank order (fp32) and write the result
+  for (size_t i = lo + threadIdx.x; i < hi; i += kThreads) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int src = 0; src < v.world; ++src)
+      add_vec(acc, __ldcg(reinterpret_cast<const uint4*>(ar_slot(v, v.rank, par, src)) + i),
+              is_half != 0);
+    out[i] = pack_vec(acc, is_half != 0);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) ar_finish(v, e);
+}
+
+unsigned long long default_timeout_ns() {
+  const char* s = getenv("B2_NVAR_TIMEOUT_MS");
+  if (s && *s) {
+    const long long ms = atoll(s);
+    if (ms > 0) return (unsigned long long)ms * 1000000ull;
+  }
+  return 10000000000ull;  // 10 s: tolerates host-side skew between ranks
+}
+
+class DeviceScope {
+ public:
+  explicit DeviceScope(int dev) {
+    cudaGetDevice(&prev_);
+    if (dev != prev_) cudaSetDevice(dev);
+  }
+  ~DeviceScope() { cudaSetDevice(prev_); }
+
+ private:
+  int prev_ = 0;
+};
+
+}  // namespace
+
+int nvar_view(b2_nvar* h, ArView* out, size_t need_slot_bytes, int* tiles_cap) {
+  if (!h) return fail(B2_ERR_STATE, "all-reduce: null handle");
+  if (!h->connected) return fail(B2_ERR_STATE, "all-reduce: handle is not connected");
+  if (need_slot_bytes > h->slot_bytes)
+    return fail(B2_ERR_INVALID_ARG, "all-reduce: payload of %zu B exceeds the slot (%zu B)",
+                need_slot_bytes, h->slot_bytes);
+  int dev = 0;
+  B2_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev != h->device)
+    return fail(B2_ERR_STATE, "all-reduce: handle belongs to device %d, current device is %d",
+                h->device, dev);
+  ArView v;
+  memset(&v, 0, sizeof(v));
+  for (int r = 0; r < h->world; ++r) v.base[r] = h->peers[r];
+  v.rank = h->rank;
+  v.world = h->world;
+  v.slot_bytes = h->slot_bytes;
+  v.timeout_ns = h->timeout_ns;
+  *out = v;
+  if (tiles_cap) *tiles_cap = kArMaxFlags;
+  return B2_OK;
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+int b2_nvar_create(int device, int rank, int world, size_t slot_bytes, b2_nvar** out) {
+  if (!out) return fail(B2_ERR_INVALID_ARG, "nvar_create: null output");
+  if (world < 1 || world > kArMaxWorld || rank < 0 || rank >= world)
+    return fail(B2_ERR_INVALID_ARG, "nvar_create: rank %d / world %d (world <= %d)", rank, world,
+                kArMaxWorld);
+  if (slot_bytes < 16) return fail(B2_ERR_INVALID_ARG, "nvar_create: slot of %zu B", slot_bytes);
+  DeviceScope scope(device);
+  slot_bytes = (slot_bytes + 255) & ~(size_t)255;
+  b2_nvar* h = new b2_nvar;
+  memset(h, 0, sizeof(*h));
+  h->device = device;
+  h->rank = rank;
+  h->world = world;
+  h->slot_bytes = slot_bytes;
+  h->bytes = kArSlotsOffset + 2 * (size_t)world * slot_bytes;
+  h->timeout_ns = default_timeout_ns();
+  cudaError_t e = cudaMalloc(&h->local, h->bytes);
+  if (e == cudaSuccess) e = cudaMemset(h->local, 0, h->bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    if (h->local) cudaFree(h->local);
+    delete h;
+    return fail(B2_ERR_CUDA, "nvar_create: %s", cudaGetErrorString(e));
+  }
+  h->peers[rank] = h->local;
+  h->connected = (world == 1);
+  *out = h;
+  return B2_OK;
+}
+
+int b2_nvar_export(const b2_nvar* h, void* handle_out) {
+  if (!h || !handle_out) return fail(B2_ERR_INVALID_ARG, "nvar_export: null argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == B2_IPC_HANDLE_BYTES, "IPC handle size");
+  DeviceScope scope(h->device);
+  cudaIpcMemHandle_t ih;
+  B2_CUDA_TRY(cudaIpcGetMemHandle(&ih, h->local));
+  memcpy(handle_out, &ih, sizeof(ih));
+  return B2_OK;
+}
+
+int b2_nvar_connect(b2_nvar* h, const void* handles) {
+  if (!h || !handles) return fail(B2_ERR_INVALID_ARG, "nvar_connect: null argument");
+  if (h->connected) return B2_OK;
+  DeviceScope scope(h->device);
+  const unsigned char* hb = static_cast<const unsigned char*>(handles);
+  for (int r = 0; r < h->world; ++r) {
+    if (r == h->rank || h->opened[r]) continue;
+    cudaIpcMemHandle_t ih;
+    memcpy(&ih, hb + (size_t)r * B2_IPC_HANDLE_BYTES, sizeof(ih));
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, ih, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess)
+      return fail(B2_ERR_CUDA, "nvar_connect: opening rank %d's buffer failed: %s", r,
+                  cudaGetErrorString(e));
+    h->peers[r] = static_cast<char*>(p);
+    h->opened[r] = true;
+  }
+  h->connected = true;
+  return B2_OK;
+}
+
+int b2_nvar_is_connected(const b2_nvar* h) { return h && h->connected ? 1 : 0; }
+
+size_t b2_nvar_max_bytes(const b2_nvar* h) { return h ? h->slot_bytes : 0; }
+
+int b2_nvar_set_timeout_ns(b2_nvar* h, uint64_t ns) {
+  if (!h || ns == 0) return fail(B2_ERR_INVALID_ARG, "nvar_set_timeout_ns: bad argument");
+  h->timeout_ns = ns;
+  return B2_OK;
+}
+
+int b2_nvar_allreduce(b2_nvar* h, const void* in, void* out, size_t count, int dtype,
+                      void* stream) {
+  if (!in || !out) return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: null pointer");
+  if (dtype != B2_DTYPE_F16 && dtype != B2_DTYPE_F32)
+    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: dtype %d (0 = f16, 1 = f32)", dtype);
+  const size_t bytes = count * (dtype == B2_DTYPE_F16 ? 2 : 4);
+  if (bytes == 0 || bytes % 16 != 0)
+    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: %zu bytes (must be a positive multiple of 16)",
+                bytes);
+  if (!aligned16(in) || !aligned16(out))
+    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: buffers must be 16-byte aligned");
+  ArView v;
+  int rc = nvar_view(h, &v, bytes, nullptr);
+  if (rc) return rc;
+  const size_t nvec = bytes / 16;
+  size_t chunk = std::max(kMinChunk, (bytes + 147) / 148);
+  chunk = (chunk + 15) & ~(size_t)15;
+  const size_t chunk_vec = chunk / 16;
+  const size_t grid = (nvec + chunk_vec - 1) / chunk_vec;
+  if (grid > (size_t)kArMaxFlags) return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: too many chunks");
+  nvar_kernel<<<(unsigned)grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(in), static_cast<uint4*>(out), nvec, chunk_vec,
+      dtype == B2_DTYPE_F16 ? 1 : 0, v);
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+
+int b2_nvar_status(b2_nvar* h, int clear, int* device_status) {
+  if (!h || !device_status) return fail(B2_ERR_INVALID_ARG, "nvar_status: null argument");
+  DeviceScope scope(h->device);
+  ArHeader hdr;
+  B2_CUDA_TRY(cudaDeviceSynchronize());
+  B2_CUDA_TRY(cudaMemcpy(&hdr, h->local, sizeof(hdr), cudaMemcpyDeviceToHost));
+  if (clear && hdr.status)
+    B2_CUDA_TRY(cudaMemset(h->local + offsetof(ArHeader, status), 0, sizeof(int)));
+  *device_status = hdr.status;
+  return B2_OK;
+}
+
+int b2_nvar_rank(const b2_nvar* h) { return h ? h->rank : -1; }
+int b2_nvar_world(const b2_nvar* h) { return h ? h->world : -1; }
+
+int b2_nvar_destroy(b2_nvar* h) {
+  if (!h) return fail(B2_ERR_INVALID_ARG, "nvar_destroy: null handle");
+  {
+    DeviceScope scope(h->device);
+    for (int r = 0; r < h->world; ++r)
+      if (h->opened[r]) cudaIpcCloseMemHandle(h->peers[r]);
+    cudaFree(h->local);
+  }
+  delete h;
+  return B2_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,92 @@
+// Layout of an NVLink all-reduce buffer and the device side of its protocol, shared by the
+// standalone all-reduce kernel and the GEMM epilogue that fuses it.
+//
+// Every rank owns one buffer (cudaMalloc, exported with CUDA IPC, mapped by every peer):
+//   [header 4 KB][flags: kArMaxWorld x kArMaxFlags u32][slots: 2 parities x world x slot_bytes]
+// header.gen counts completed launches on this rank. A launch uses generation e = gen + 1 and
+// slot parity e & 1. A rank writes its contribution for piece `idx` (a chunk or an output tile)
+// into slot[e & 1][rank] of every rank, then stores flag[rank][idx] = e with release semantics on
+// every rank. Readers acquire flag[src][idx] >= e for all src, then add the slots in rank order
+// 0..world-1 in fp32, so all ranks produce bit-identical sums. A slot parity is reused only at
+// e + 2, which a rank reaches only after every peer has published e + 1, which each peer does only
+// after finishing launch e (stream order) - so no slot is overwritten while it is read
+// (the argument of kernels/hostar.cu:9-14, for `world` ranks).
+#pragma once
+
+#include "b2_device.cuh"
+
+namespace b2 {
+
+constexpr int kArMaxWorld = 8;
+constexpr int kArMaxFlags = 4096;
+constexpr size_t kArHeaderBytes = 4096;
+constexpr size_t kArFlagsBytes = (size_t)kArMaxWorld * kArMaxFlags * sizeof(uint32_t);
+constexpr size_t kArSlotsOffset = kArHeaderBytes + kArFlagsBytes;
+
+struct ArHeader {
+  uint32_t gen;   // completed launches
+  uint32_t done;  // CTAs of the running launch that finished
+  int status;     // 0 or B2_ERR_TIMEOUT
+};
+
+// Kernel-parameter view of one all-reduce handle.
+struct ArView {
+  char* base[kArMaxWorld];  // base[r]: rank r's buffer as mapped in this process
+  int rank;
+  int world;
+  unsigned long long slot_bytes;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ ArHeader* ar_header(const ArView& v) {
+  return reinterpret_cast<ArHeader*>(v.base[v.rank]);
+}
+__device__ __forceinline__ uint32_t* ar_flag(const ArView& v, int owner, int src, int idx) {
+  return reinterpret_cast<uint32_t*>(v.base[owner] + kArHeaderBytes) + (size_t)src * kArMaxFlags +
+         idx;
+}
+__device__ __forceinline__ char* ar_slot(const ArView& v, int owner, int parity, int src) {
+  return v.base[owner] + kArSlotsOffset + ((size_t)parity * v.world + src) * v.slot_bytes;
+}
+
+// Generation of the launch in progress (called by one thread).
+__device__ __forceinline__ uint32_t ar_begin(const ArView& v) {
+  return *reinterpret_cast<volatile uint32_t*>(&ar_header(v)->gen) + 1u;
+}
+
+// Publish piece `idx` of generation e on every rank. Call after this CTA's data stores and a
+// __threadfence_system() by every storing thread, from one thread.
+__device__ __forceinline__ void ar_publish(const ArView& v, int idx, uint32_t e) {
+  for (int r = 0; r < v.world; ++r) st_release_sys(ar_flag(v, r, v.rank, idx), e);
+}
+
+// Wait until every rank has published piece `idx` of generation e here. Bounded: after
+// v.timeout_ns records B2_ERR_TIMEOUT in the header and returns false. One thread.
+__device__ __forceinline__ bool ar_wait(const ArView& v, int idx, uint32_t e) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (int src = 0; src < v.world; ++src) {
+    const uint32_t* f = ar_flag(v, v.rank, src, idx);
+    unsigned int it = 0;
+    while ((int)(ld_acquire_sys(f) - e) < 0) {
+      if (++it >= kMaxSpin || globaltimer_ns() - t0 > v.timeout_ns) {
+        atomicCAS(&ar_header(v)->status, 0, B2_ERR_TIMEOUT);
+        return false;
+      }
+      if ((it & 15u) == 0) __nanosleep(64);
+    }
+  }
+  return true;
+}
+
+// Count this CTA as finished; the last CTA of the launch advances the generation. One thread,
+// after the CTA's last use of the buffer.
+__device__ __forceinline__ void ar_finish(const ArView& v, uint32_t e) {
+  ArHeader* h = ar_header(v);
+  __threadfence();
+  if (atomicAdd(&h->done, 1u) == gridDim.x - 1) {
+    atomicExch(&h->done, 0u);
+    atomicExch(&h->gen, e);
+  }
+}
+
+}  // namespace b2

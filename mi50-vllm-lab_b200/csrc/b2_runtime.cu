@@ -1,0 +1,260 @@
+// Host runtime of the library: status strings, error detail, device properties, tensor-map
+// encoding, workspace management, tuning knobs and the shared-memory rendezvous registry.
+#include <cudaTypedefs.h>
+#include <fcntl.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+
+#include "b2_device.cuh"
+#include "b2_internal.h"
+
+namespace b2 {
+
+static thread_local char g_last_error[512] = "";
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+// ----------------------------------------------------------------------------------------------
+// Device properties
+// ----------------------------------------------------------------------------------------------
+static std::mutex g_dev_mu;
+static DeviceInfo g_dev[64];
+
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  B2_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(B2_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ok) {
+    cudaDeviceProp p;
+    B2_CUDA_TRY(cudaGetDeviceProperties(&p, dev));
+    d.sm_count = p.multiProcessorCount;
+    d.major = p.major;
+    d.minor = p.minor;
+    d.smem_optin = p.sharedMemPerBlockOptin;
+    d.ok = true;
+  }
+  *out = d;
+  if (d.major != 10)
+    return fail(B2_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", dev,
+                d.major, d.minor);
+  return B2_OK;
+}
+
+// ----------------------------------------------------------------------------------------------
+// Tensor maps (driver entry point fetched through the runtime; no link-time libcuda dependency)
+// ----------------------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+              uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swizzle) {
+  auto fn = get_encode_fn();
+  if (!fn) return fail(B2_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B2_ERR_INVALID_ARG,
+                "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, stride %llu B, box %u x %u",
+                (int)r, (unsigned long long)inner, (unsigned long long)outer,
+                (unsigned long long)row_stride_bytes, box_inner, box_outer);
+  return B2_OK;
+}
+
+// ----------------------------------------------------------------------------------------------
+// Workspace
+// ----------------------------------------------------------------------------------------------
+size_t ws_counters_offset() { return kWsStatusBytes; }
+size_t ws_partials_offset() {
+  size_t off = kWsStatusBytes + (size_t)kWsMaxTiles * sizeof(int);
+  return (off + 255) & ~(size_t)255;
+}
+size_t ws_total_bytes() {
+  return ws_partials_offset() + (size_t)kWsMaxCtas * 2 * kSlotFloats * sizeof(float);
+}
+
+// ----------------------------------------------------------------------------------------------
+// Tuning
+// ----------------------------------------------------------------------------------------------
+static std::atomic<int> g_tune[8];
+
+int tuning(int key) { return (key >= 0 && key < 8) ? g_tune[key].load() : 0; }
+
+int streamk_ctas(long long total, int sm_count, int occ, int min_units_default) {
+  int cps = tuning(B2_TUNE_CTAS_PER_SM);
+  if (cps <= 0 || cps > occ) cps = occ;
+  int min_units = tuning(B2_TUNE_MIN_UNITS);
+  if (min_units <= 0) min_units = min_units_default;
+  long long cap = (long long)sm_count * cps;
+  long long by_units = (total + min_units - 1) / min_units;
+  long long c = std::min(std::min(cap, by_units), total);
+  c = std::min<long long>(c, kWsMaxCtas);
+  return (int)std::max<long long>(c, 1);
+}
+
+}  // namespace b2
+
+using namespace b2;
+
+extern "C" {
+
+const char* b2_status_string(int status) {
+  switch (status) {
+    case B2_OK: return "ok";
+    case B2_ERR_INVALID_ARG: return "invalid argument";
+    case B2_ERR_UNSUPPORTED: return "unsupported device or configuration";
+    case B2_ERR_CUDA: return "CUDA error";
+    case B2_ERR_WORKSPACE: return "workspace missing or too small";
+    case B2_ERR_TIMEOUT: return "device-side wait timed out";
+    case B2_ERR_STATE: return "bad handle or state";
+    default: return "unknown status";
+  }
+}
+
+const char* b2_last_error(void) { return g_last_error; }
+
+int b2_abi_version(void) { return B2_ABI_VERSION; }
+
+size_t b2_workspace_bytes(int device) {
+  (void)device;
+  return ws_total_bytes();
+}
+
+int b2_workspace_init(void* ws, size_t ws_bytes, void* stream) {
+  if (!ws || ws_bytes < ws_total_bytes())
+    return fail(B2_ERR_WORKSPACE, "workspace of %zu B, need %zu B", ws_bytes, ws_total_bytes());
+  // Only the status words and the counters must start at zero; the slots are overwritten.
+  B2_CUDA_TRY(cudaMemsetAsync(ws, 0, ws_partials_offset(), (cudaStream_t)stream));
+  return B2_OK;
+}
+
+int b2_workspace_status(void* ws, int clear, int* device_status) {
+  if (!ws || !device_status) return fail(B2_ERR_INVALID_ARG, "null workspace or output");
+  int v = 0;
+  B2_CUDA_TRY(cudaDeviceSynchronize());
+  B2_CUDA_TRY(cudaMemcpy(&v, ws, sizeof(int), cudaMemcpyDeviceToHost));
+  if (clear && v) B2_CUDA_TRY(cudaMemset(ws, 0, sizeof(int)));
+  *device_status = v;
+  return B2_OK;
+}
+
+int b2_set_tuning(int key, int value) {
+  if (key < 0 || key >= 8) return fail(B2_ERR_INVALID_ARG, "unknown tuning key %d", key);
+  g_tune[key].store(value);
+  return B2_OK;
+}
+
+int b2_get_tuning(int key) { return tuning(key); }
+
+// ----------------------------------------------------------------------------------------------
+// Rendezvous registry in POSIX shared memory
+// ----------------------------------------------------------------------------------------------
+}  // extern "C"
+
+namespace {
+constexpr uint32_t kRegMagic = 0x42325247u;  // "B2RG"
+constexpr int kRegMaxWorld = 64;
+struct RegLayout {
+  uint32_t magic;
+  uint32_t world;
+  uint32_t present[kRegMaxWorld];
+  unsigned char blob[kRegMaxWorld][B2_BLOB_BYTES];
+};
+}  // namespace
+
+struct b2_registry {
+  RegLayout* map;
+  int world;
+};
+
+extern "C" {
+
+int b2_registry_open(const char* name, int world, int create, b2_registry** out) {
+  if (!name || !out || world < 1 || world > kRegMaxWorld)
+    return fail(B2_ERR_INVALID_ARG, "registry: bad name/world (%d)", world);
+  const int fd = shm_open(name, create ? (O_CREAT | O_RDWR) : O_RDWR, 0600);
+  if (fd < 0) return fail(B2_ERR_STATE, "registry: shm_open(%s) failed", name);
+  if (create && ftruncate(fd, sizeof(RegLayout)) != 0) {
+    close(fd);
+    return fail(B2_ERR_STATE, "registry: ftruncate(%s) failed", name);
+  }
+  void* p = mmap(nullptr, sizeof(RegLayout), PROT_READ | PROT_WRITE, MAP_SHARED, fd, 0);
+  close(fd);
+  if (p == MAP_FAILED) return fail(B2_ERR_STATE, "registry: mmap(%s) failed", name);
+  RegLayout* r = static_cast<RegLayout*>(p);
+  if (create) {
+    memset(r, 0, sizeof(RegLayout));
+    r->world = (uint32_t)world;
+    __atomic_store_n(&r->magic, kRegMagic, __ATOMIC_RELEASE);
+  } else if (__atomic_load_n(&r->magic, __ATOMIC_ACQUIRE) != kRegMagic ||
+             r->world != (uint32_t)world) {
+    munmap(p, sizeof(RegLayout));
+    return fail(B2_ERR_STATE, "registry %s is not initialised for world %d", name, world);
+  }
+  *out = new b2_registry{r, world};
+  return B2_OK;
+}
+
+int b2_registry_put(b2_registry* reg, int rank, const void* blob) {
+  if (!reg || !blob || rank < 0 || rank >= reg->world)
+    return fail(B2_ERR_INVALID_ARG, "registry_put: bad rank %d", rank);
+  memcpy(reg->map->blob[rank], blob, B2_BLOB_BYTES);
+  __atomic_store_n(&reg->map->present[rank], 1u, __ATOMIC_RELEASE);
+  return B2_OK;
+}
+
+int b2_registry_get(b2_registry* reg, int rank, void* blob_out) {
+  if (!reg || !blob_out || rank < 0 || rank >= reg->world)
+    return fail(B2_ERR_INVALID_ARG, "registry_get: bad rank %d", rank);
+  if (__atomic_load_n(&reg->map->present[rank], __ATOMIC_ACQUIRE) != 1u)
+    return fail(B2_ERR_STATE, "registry_get: rank %d has not published", rank);
+  memcpy(blob_out, reg->map->blob[rank], B2_BLOB_BYTES);
+  return B2_OK;
+}
+
+int b2_registry_close(b2_registry* reg) {
+  if (!reg) return fail(B2_ERR_INVALID_ARG, "registry_close: null");
+  munmap(reg->map, sizeof(RegLayout));
+  delete reg;
+  return B2_OK;
+}
+
+int b2_registry_unlink(const char* name) {
+  if (!name) return fail(B2_ERR_INVALID_ARG, "registry_unlink: null name");
+  shm_unlink(name);
+  return B2_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,505 @@
+// W4A16 skinny GEMM for sm_100a over GPTQ/Exllama-shuffled 4-bit weights, 1 <= M <= 8.
+//
+// Replaces w4_gemm / w4_skinny_s_kernel / w4_reduce_kernel of kernels/w4.cu:154-346,479-504 with
+// the same operand layouts (kernels/w4.cu:477-478): a [M,K] fp16, qw [K/8,N] int32, qz [K/G,N/8]
+// int32 (v2 zeros), sc [K/G,N] fp16. Design:
+//   - a producer warp streams 128-column x 128-k units (8 KB of qw plus that unit's scale and
+//     zero rows) into a ring of shared-memory stages with TMA (128-byte swizzle for qw,
+//     L2 evict-first);
+//   - each of four consumer warps owns 32 columns of the unit. A lane reads one 16-byte chunk
+//     (4 columns of one 8-k word row) per 32 k, unpacks the 8 nibbles of each word to
+//     (q - z) in fp16 exactly (magic-number 1024 trick with zero constants built from integer
+//     bits) and feeds them to mma.sync m16n8k16 as the A operand against the <= 8 activation
+//     rows (B operand). Each weight is dequantized once and used for all M rows.
+//   - (q - z) * x is accumulated per quantization group in fp32 and multiplied by the group's
+//     scale in fp32 once per group, so no product is rounded to fp16 (the reference rounds
+//     (q - z) * s to fp16 per weight, kernels/w4.cu:33-36).
+//   - stream-K over a persistent grid; tiles shared by CTAs are summed by the last CTA to
+//     finish, in CTA order, from fp32 slots (one launch; replaces the workspace + second
+//     reduce kernel of kernels/w4.cu:154-166,330-346).
+//   - optionally the NVLink all-reduce of a row-parallel layer is fused into the epilogue: the
+//     finished fp32 tile is pushed to every rank, and each rank adds the ranks' tiles in rank
+//     order (bit-identical on every rank).
+#include <cuda_fp16.h>
+
+#include "b2_device.cuh"
+#include "b2_internal.h"
+#include "b2_nvar.cuh"
+
+namespace b2 {
+
+int nvar_view(b2_nvar* ar, ArView* out, size_t need_slot_bytes, int* tiles_cap);
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = (kWarps + 1) * 32;
+constexpr int kUnitK = 128;                 // k per unit = 16 word rows
+constexpr int kQwBox = 16 * 128;            // 16 word rows x 32 columns x 4 B (one TMA box)
+constexpr int kQwStage = kWarps * kQwBox;   // 8 KB
+constexpr int kStages = 8;
+
+template <int GP>  // GP: 32-k pairs per scale group inside a unit (1: G=32, 2: G=64, 4: G>=128)
+struct Cfg {
+  static constexpr int RG = 4 / GP;                        // group rows per unit
+  static constexpr int kScBytes = RG * kTileN * 2;         // scales of one unit
+  static constexpr int kQzBytes = RG * (kTileN / 8) * 4;   // zeros of one unit
+  static constexpr int kTx = kQwStage + kScBytes + kQzBytes;
+  static constexpr int kSmem =
+      1024 + kStages * (kQwStage + kScBytes + kQzBytes) + 2 * kStages * 8 + 32;
+};
+
+struct W4Args {
+  const __half* x;
+  __half* y;
+  int M, K, N, G;
+  StreamK sk;
+  float* partials;
+  int* counters;
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;  // (a & b) | c
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+__device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// (q - z) for the 8 nibbles of one shuffled word, as four fp16 pairs in k order
+// (k0,k1) (k2,k3) (k4,k5) (k6,k7). Nibble i sits at bits 4i (k = 2i) and nibble 4+i at bits
+// 16+4i (k = 2i+1). OR-ing a nibble into the mantissa of fp16 1024.0 (0x6400) gives 1024 + q for
+// the low nibble of a byte and 1024 + 16q for the high one. zlo = -(1024 + z) and
+// zhi = -(64 + z) in both halves; all steps are exact in fp16.
+__device__ __forceinline__ void dequant_word(uint32_t q, uint32_t zlo, uint32_t zhi,
+                                             uint32_t (&d)[4]) {
+  constexpr uint32_t kMagic = 0x64006400u;      // 1024.0 | 1024.0
+  constexpr uint32_t kSixteenth = 0x2C002C00u;  // 0.0625 | 0.0625
+  const uint32_t lo0 = lop_and_or(q, 0x000F000Fu, kMagic);
+  const uint32_t hi0 = lop_and_or(q, 0x00F000F0u, kMagic);
+  const uint32_t q8 = q >> 8;
+  const uint32_t lo1 = lop_and_or(q8, 0x000F000Fu, kMagic);
+  const uint32_t hi1 = lop_and_or(q8, 0x00F000F0u, kMagic);
+  d[0] = hadd2_u(lo0, zlo);
+  d[1] = hfma2_u(hi0, kSixteenth, zhi);
+  d[2] = hadd2_u(lo1, zlo);
+  d[3] = hfma2_u(hi1, kSixteenth, zhi);
+}
+
+// Lane output layout of a 128-column tile: lane (g, t) of warp w owns columns
+// w*32 + 4*ch(g) .. +3 for rows m = 2t (v[0]) and m = 2t+1 (v[1]).
+__device__ __forceinline__ void store_y(const W4Args& p, int tile, int colw, int t,
+                                        const float4 (&v)[2]) {
+  const int n = tile * kTileN + colw;
+  if (n >= p.N) return;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int m = 2 * t + j;
+    if (m >= p.M) continue;
+    __half2 h0 = __floats2half2_rn(v[j].x, v[j].y);
+    __half2 h1 = __floats2half2_rn(v[j].z, v[j].w);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&h0);
+    u.y = *reinterpret_cast<uint32_t*>(&h1);
+    *reinterpret_cast<uint2*>(p.y + (size_t)m * p.N + n) = u;
+  }
+}
+
+template <int GP, bool FUSED>
+__global__ void __launch_bounds__(kThreads) w4_kernel(const __grid_constant__ CUtensorMap tm_qw,
+                                                      const __grid_constant__ CUtensorMap tm_sc,
+                                                      const __grid_constant__ CUtensorMap tm_qz,
+                                                      const W4Args p, const ArView ar) {
+  using C = Cfg<GP>;
+  constexpr int RG = C::RG;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* s_qw = smem;
+  __half* s_sc = reinterpret_cast<__half*>(smem + kStages * kQwStage);
+  uint32_t* s_qz = reinterpret_cast<uint32_t*>(smem + kStages * (kQwStage + C::kScBytes));
+  uint64_t* full =
+      reinterpret_cast<uint64_t*>(smem + kStages * (kQwStage + C::kScBytes + C::kQzBytes));
+  uint64_t* empty = full + kStages;
+  volatile int* s_abort = reinterpret_cast<volatile int*>(empty + kStages);
+  volatile int* s_flag = s_abort + 1;
+  volatile uint32_t* s_gen = reinterpret_cast<volatile uint32_t*>(s_abort + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const StreamK& sk = p.sk;
+  const long long u_lo = sk_begin(sk, blockIdx.x), u_hi = sk_begin(sk, blockIdx.x + 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarps);
+    }
+    *s_abort = 0;
+    *s_flag = 0;
+    if (FUSED) *s_gen = ar_begin(ar);
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------------ producer warp (1 thread)
+  if (warp == kWarps) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qw);
+      tma_prefetch_desc(&tm_sc);
+      tma_prefetch_desc(&tm_qz);
+      const uint64_t pol = l2_evict_first_policy();
+      int st = 0;
+      uint32_t ph = 0;
+      uint32_t last_ph[kStages];
+      bool used[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) used[s] = false, last_ph[s] = 0;
+      for (long long u = u_lo; u < u_hi; ++u) {
+        if (!mbar_wait(&empty[st], ph ^ 1u, s_abort)) break;
+        const int tile = (int)(u / sk.upt), ku = (int)(u % sk.upt);
+        const int n0 = tile * kTileN;
+        const int grow = (ku * kUnitK) / p.G;
+        mbar_arrive_expect_tx(&full[st], C::kTx);
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w)
+          tma_load_2d(s_qw + st * kQwStage + w * kQwBox, &tm_qw, &full[st], n0 + 32 * w, ku * 16,
+                      pol);
+        tma_load_2d(s_sc + st * (RG * kTileN), &tm_sc, &full[st], n0, grow, pol);
+        tma_load_2d(s_qz + st * (RG * kTileN / 8), &tm_qz, &full[st], n0 / 8, grow, pol);
+        used[st] = true;
+        last_ph[st] = ph;
+        if (++st == kStages) st = 0, ph ^= 1u;
+      }
+      for (int s = 0; s < kStages; ++s) {
+        if (!used[s]) continue;
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_test(&full[s], last_ph[s]) && globaltimer_ns() - t0 < kPipeWaitNs) {
+        }
+      }
+      if (*s_abort) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumer warps
+  const int g = lane >> 2, t = lane & 3;
+  const int ch = ((g & 1) << 2) | (g >> 1);  // 16-byte chunk (4 columns) of the 128-byte row
+  const int colw = warp * 32 + ch * 4;       // lane's first column inside the tile
+  const bool has_row = g < p.M;
+  const __half* xrow = p.x + (size_t)(has_row ? g : 0) * p.K;
+  const uint32_t e = FUSED ? *s_gen : 0u;
+
+  float acc[2][4], accg[2][4];
+#pragma unroll
+  for (int T = 0; T < 2; ++T)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[T][i] = accg[T][i] = 0.f;
+
+  int st = 0;
+  uint32_t ph = 0;
+  bool ok = true;
+  for (long long u = u_lo; u < u_hi; ++u) {
+    const int tile = (int)(u / sk.upt), ku = (int)(u % sk.upt);
+    uint4 xv[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      xv[q] = has_row ? ldg_nc128(xrow + ku * kUnitK + 32 * q + 8 * t) : make_uint4(0, 0, 0, 0);
+    if (ok) ok = mbar_wait(&full[st], ph, s_abort);
+
+    // zero constants and scales of the lane's 4 columns for each group row of the unit
+    uint32_t zlo[RG][4], zhi[RG][4];
+    float scl[RG][4];
+#pragma unroll
+    for (int r = 0; r < RG; ++r) {
+      const uint32_t zw = s_qz[(st * RG + r) * (kTileN / 8) + (colw >> 3)] >> ((colw & 7) * 4);
+      const uint2 sv = *reinterpret_cast<const uint2*>(s_sc + (st * RG + r) * kTileN + colw);
+      const __half2 s01 = *reinterpret_cast<const __half2*>(&sv.x);
+      const __half2 s23 = *reinterpret_cast<const __half2*>(&sv.y);
+      scl[r][0] = __low2float(s01);
+      scl[r][1] = __high2float(s01);
+      scl[r][2] = __low2float(s23);
+      scl[r][3] = __high2float(s23);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t z = (zw >> (4 * i)) & 0xFu;
+        zlo[r][i] = (0xE400u + z) * 0x00010001u;         // -(1024 + z)
+        zhi[r][i] = (0xD400u + (z << 4)) * 0x00010001u;  // -(64 + z)
+      }
+    }
+
+    const uint32_t qb = smem_u32(s_qw + st * kQwStage + warp * kQwBox);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // 32-k pair q: word rows 4q..4q+3, lane t takes row 4q+t
+      const int row = 4 * q + t;
+      const uint4 w = lds128(qb + row * 128 + ((ch ^ (row & 7)) << 4));
+      const int r = (RG == 1) ? 0 : (q / GP);
+      uint32_t d0[4], d1[4], d2[4], d3[4];
+      dequant_word(w.x, zlo[r][0], zhi[r][0], d0);
+      dequant_word(w.y, zlo[r][1], zhi[r][1], d1);
+      dequant_word(w.z, zlo[r][2], zhi[r][2], d2);
+      dequant_word(w.w, zlo[r][3], zhi[r][3], d3);
+      // n-tile 0: A rows g / g+8 = columns colw / colw+1; n-tile 1: colw+2 / colw+3
+      mma_16816(accg[0], d0[0], d1[0], d0[1], d1[1], xv[q].x, xv[q].y);
+      mma_16816(accg[0], d0[2], d1[2], d0[3], d1[3], xv[q].z, xv[q].w);
+      mma_16816(accg[1], d2[0], d3[0], d2[1], d3[1], xv[q].x, xv[q].y);
+      mma_16816(accg[1], d2[2], d3[2], d2[3], d3[3], xv[q].z, xv[q].w);
+      if ((q + 1) % GP == 0) {
+#pragma unroll
+        for (int T = 0; T < 2; ++T)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[T][i] = fmaf(scl[r][2 * T + (i >> 1)], accg[T][i], acc[T][i]);
+            accg[T][i] = 0.f;
+          }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (++st == kStages) st = 0, ph ^= 1u;
+
+    if (ku != sk.upt - 1 && u != u_hi - 1) continue;
+    // ---------------------------------------------------------------- end of a tile segment
+    float4 v[2];
+    v[0] = make_float4(acc[0][0], acc[0][2], acc[1][0], acc[1][2]);  // m = 2t
+    v[1] = make_float4(acc[0][1], acc[0][3], acc[1][1], acc[1][3]);  // m = 2t + 1
+#pragma unroll
+    for (int T = 0; T < 2; ++T)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[T][i] = 0.f;
+
+    const long long ts = (long long)tile * sk.upt;
+    const int first = sk_owner(sk, ts), last = sk_owner(sk, ts + sk.upt - 1);
+    bool finisher = true;
+    if (first != last) {
+      float* slot =
+          p.partials + ((size_t)blockIdx.x * 2 + sk_slot(sk, blockIdx.x, tile)) * kSlotFloats;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        if (2 * t + j < p.M)
+          __stcg(reinterpret_cast<float4*>(slot + (2 * t + j) * kTileN + colw), v[j]);
+      __threadfence();
+      named_bar_sync(1, kWarps * 32);
+      if (threadIdx.x == 0) {
+        const int prev = atomicAdd(&p.counters[tile], 1);
+        const int fin = (prev == last - first);
+        if (fin) atomicExch(&p.counters[tile], 0);
+        *s_flag = fin;
+      }
+      named_bar_sync(1, kWarps * 32);
+      finisher = *s_flag != 0;
+      if (finisher) {
+        __threadfence();
+        v[0] = v[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = first; c <= last; ++c) {
+          const float* sl = p.partials + ((size_t)c * 2 + sk_slot(sk, c, tile)) * kSlotFloats;
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            if (2 * t + j < p.M) {
+              const float4 a = __ldcg(reinterpret_cast<const float4*>(sl + (2 * t + j) * kTileN + colw));
+              v[j].x += a.x;
+              v[j].y += a.y;
+              v[j].z += a.z;
+              v[j].w += a.w;
+            }
+        }
+      }
+    }
+    if (!finisher) continue;
+    if (!FUSED) {
+      store_y(p, tile, colw, t, v);
+      continue;
+    }
+    // Fused all-reduce: push this rank's finished fp32 tile into slot[e&1][rank] of every rank
+    // ([M][N] fp32 layout), then publish the tile's flag on every rank.
+    const int n = tile * kTileN + colw;
+    if (n < p.N) {
+      for (int r = 0; r < ar.world; ++r) {
+        float* dst = reinterpret_cast<float*>(ar_slot(ar, r, e & 1u, ar.rank));
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          if (2 * t + j < p.M) *reinterpret_cast<float4*>(dst + (size_t)(2 * t + j) * p.N + n) = v[j];
+      }
+    }
+    __threadfence_system();
+    named_bar_sync(1, kWarps * 32);
+    if (threadIdx.x == 0) ar_publish(ar, tile, e);
+  }
+  if (!ok && lane == 0) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
+  if (!FUSED) return;
+
+  // ------------------------------------------------------------------ fused all-reduce, phase 2
+  // CTA b adds tiles b, b + grid, ... over all ranks in rank order and writes the fp16 result.
+  for (int tile = blockIdx.x; tile < sk.tiles; tile += gridDim.x) {
+    named_bar_sync(1, kWarps * 32);
+    if (threadIdx.x == 0) *s_flag = ar_wait(ar, tile, e) ? 1 : 0;
+    named_bar_sync(1, kWarps * 32);
+    __threadfence();
+    const int n = tile * kTileN + colw;
+    if (n >= p.N) continue;
+    float4 v[2];
+    v[0] = v[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int src = 0; src < ar.world; ++src) {
+      const float* sl = reinterpret_cast<const float*>(ar_slot(ar, ar.rank, e & 1u, src));
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        if (2 * t + j < p.M) {
+          const float4 a = __ldcg(reinterpret_cast<const float4*>(sl + (size_t)(2 * t + j) * p.N + n));
+          v[j].x += a.x;
+          v[j].y += a.y;
+          v[j].z += a.z;
+          v[j].w += a.w;
+        }
+    }
+    store_y(p, tile, colw, t, v);
+  }
+  named_bar_sync(1, kWarps * 32);
+  if (threadIdx.x == 0) ar_finish(ar, e);
+}
+
+struct KernelCache {
+  bool configured = false;
+  int occ = 0;
+};
+KernelCache g_cache[64][3][2];
+
+template <int GP, bool FUSED>
+int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, const ArView* ar,
+           cudaStream_t stream) {
+  using C = Cfg<GP>;
+  W4Args a = a0;
+  DeviceInfo di;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  int dev = 0;
+  B2_CUDA_TRY(cudaGetDevice(&dev));
+  auto kern = w4_kernel<GP, FUSED>;
+  KernelCache& kc = g_cache[dev][GP == 1 ? 0 : GP == 2 ? 1 : 2][FUSED ? 1 : 0];
+  if (!kc.configured) {
+    B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+    B2_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&kc.occ, kern, kThreads, C::kSmem));
+    if (kc.occ < 1) return fail(B2_ERR_UNSUPPORTED, "w4: kernel does not fit on an SM");
+    kc.configured = true;
+  }
+  const int K = a.K, N = a.N, G = a.G;
+  StreamK sk;
+  sk.upt = K / kUnitK;
+  sk.tiles = (N + kTileN - 1) / kTileN;
+  sk.total = (long long)sk.tiles * sk.upt;
+  sk.ctas = streamk_ctas(sk.total, di.sm_count, kc.occ, 4);
+  if (FUSED) {
+    // Every CTA must be resident at once: a CTA waiting for peers must not hold back another
+    // CTA of the same launch.
+    sk.ctas = std::min(sk.ctas, di.sm_count * kc.occ);
+  }
+  a.sk = sk;
+
+  CUtensorMap m_qw, m_sc, m_qz;
+  rc = encode_2d(&m_qw, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, (uint64_t)N, (uint64_t)(K / 8),
+                 (uint64_t)N * 4, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(&m_sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, (uint64_t)N, (uint64_t)(K / G),
+                 (uint64_t)N * 2, kTileN, C::RG, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  rc = encode_2d(&m_qz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, (uint64_t)(N / 8), (uint64_t)(K / G),
+                 (uint64_t)N / 2, kTileN / 8, C::RG, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  ArView none{};
+  kern<<<sk.ctas, kThreads, C::kSmem, stream>>>(m_qw, m_sc, m_qz, a, ar ? *ar : none);
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+
+int validate(const void* a, const void* qw, const void* qz, const void* sc, const void* y, int M,
+             int K, int N, int G, const void* ws, size_t ws_bytes) {
+  if (!a || !qw || !qz || !sc || !y) return fail(B2_ERR_INVALID_ARG, "w4: null pointer");
+  if (M < 1 || M > kMaxM) return fail(B2_ERR_INVALID_ARG, "w4: M=%d outside 1..8", M);
+  if (K < kUnitK || K % kUnitK != 0)
+    return fail(B2_ERR_INVALID_ARG, "w4: K=%d must be a positive multiple of 128", K);
+  if (N < 32 || N % 32 != 0)
+    return fail(B2_ERR_INVALID_ARG, "w4: N=%d must be a positive multiple of 32", N);
+  if (!(G == 32 || G == 64 || (G >= 128 && G % 128 == 0)) || K % G != 0)
+    return fail(B2_ERR_INVALID_ARG,
+                "w4: group size %d unsupported (32, 64 or a multiple of 128 dividing K=%d)", G, K);
+  if (!aligned16(a) || !aligned16(qw) || !aligned16(qz) || !aligned16(sc))
+    return fail(B2_ERR_INVALID_ARG, "w4: a, qw, qz and sc must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(y) & 7u) != 0)
+    return fail(B2_ERR_INVALID_ARG, "w4: y must be 8-byte aligned");
+  if ((N + kTileN - 1) / kTileN > kWsMaxTiles) return fail(B2_ERR_INVALID_ARG, "w4: N=%d too large", N);
+  if (!ws || ws_bytes < ws_total_bytes())
+    return fail(B2_ERR_WORKSPACE, "w4: workspace of %zu B, need %zu B", ws_bytes, ws_total_bytes());
+  return B2_OK;
+}
+
+W4Args make_args(const void* a, void* y, int M, int K, int N, int G, void* ws) {
+  W4Args r;
+  r.x = static_cast<const __half*>(a);
+  r.y = static_cast<__half*>(y);
+  r.M = M;
+  r.K = K;
+  r.N = N;
+  r.G = G;
+  char* wsb = static_cast<char*>(ws);
+  r.status = reinterpret_cast<int*>(wsb);
+  r.counters = reinterpret_cast<int*>(wsb + ws_counters_offset());
+  r.partials = reinterpret_cast<float*>(wsb + ws_partials_offset());
+  return r;
+}
+
+template <bool FUSED>
+int dispatch(const W4Args& args, const void* qw, const void* qz, const void* sc, const ArView* ar,
+             cudaStream_t stream) {
+  switch (args.G) {
+    case 32: return launch<1, FUSED>(args, qw, qz, sc, ar, stream);
+    case 64: return launch<2, FUSED>(args, qw, qz, sc, ar, stream);
+    default: return launch<4, FUSED>(args, qw, qz, sc, ar, stream);
+  }
+}
+
+}  // namespace
+
+int launch_w4(const void* a, const void* qw, const void* qz, const void* sc, void* y, int M, int K,
+              int N, int G, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  int rc = validate(a, qw, qz, sc, y, M, K, N, G, ws, ws_bytes);
+  if (rc) return rc;
+  return dispatch<false>(make_args(a, y, M, K, N, G, ws), qw, qz, sc, nullptr, stream);
+}
+
+int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* qz, const void* sc,
+                        void* y, int M, int K, int N, int G, void* ws, size_t ws_bytes,
+                        cudaStream_t stream) {
+  int rc = validate(a, qw, qz, sc, y, M, K, N, G, ws, ws_bytes);
+  if (rc) return rc;
+  ArView v;
+  int tiles_cap = 0;
+  rc = nvar_view(h, &v, (size_t)M * N * sizeof(float), &tiles_cap);
+  if (rc) return rc;
+  if ((N + kTileN - 1) / kTileN > tiles_cap)
+    return fail(B2_ERR_INVALID_ARG, "w4_allreduce: N=%d has more tiles than flags", N);
+  return dispatch<true>(make_args(a, y, M, K, N, G, ws), qw, qz, sc, &v, stream);
+}
+
+}  // namespace b2
+
+extern "C" int b2_w4_gemm(const void* a, const void* qw, const void* qz, const void* sc, void* y,
+                          int M, int K, int N, int group_size, void* ws, size_t ws_bytes,
+                          void* stream) {
+  return b2::launch_w4(a, qw, qz, sc, y, M, K, N, group_size, ws, ws_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b2_w4_gemm_allreduce(b2_nvar* ar, const void* a, const void* qw, const void* qz,
+                                    const void* sc, void* y, int M, int K, int N, int group_size,
+                                    void* ws, size_t ws_bytes, void* stream) {
+  if (!ar) return b2::fail(B2_ERR_STATE, "w4_allreduce: null all-reduce handle");
+  return b2::launch_w4_allreduce(ar, a, qw, qz, sc, y, M, K, N, group_size, ws, ws_bytes,
+                                 static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,100 @@
+"""fp16 skinny GEMM on the GPU against the oracle (kernels/bench_skinny.py:44 in float64)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from gpu_util import check, dev, f16_ref_sampled, sample_columns, stream_ptr, workspace
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("path", sorted(GOLDEN.glob("f16_*.npz")), ids=lambda p: p.stem)
+def test_golden(ops, oracle, path):
+    d = np.load(path)
+    y = ops.gemm(dev(d["x"]), dev(d["w"]), 20)
+    check(y, d["ref"].astype(np.float64), path.stem)
+    check(y, oracle.gemm_ref(d["x"], d["w"]), path.stem)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("K,N", [(512, 1000), (5120, 1387), (1032, 128), (64, 129), (8, 7),
+                                 (4096, 256), (2056, 300)])
+def test_shapes(ops, oracle, M, K, N):
+    x, w = oracle.gen_f16(M, K, N, seed=M * 1000 + K + N)
+    y = ops.gemm(dev(x), dev(w), 0)
+    assert y.shape == (M, N) and y.dtype == torch.float16
+    check(y, oracle.gemm_ref(x, w), f"M={M} K={K} N={N}")
+
+
+def test_config1_lm_head_sampled_columns(ops):
+    """M=7, K=5120, N=151936 (1.56 GB of weights)."""
+    g = torch.Generator(device="cuda").manual_seed(101)
+    M, K, N = 7, 5120, 151936
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    y = ops.gemm(x, w, 20)
+    assert torch.isfinite(y).all()
+    cols = sample_columns(N, 1500, seed=5)
+    check(y[:, torch.from_numpy(cols).cuda()], f16_ref_sampled(x, w, cols), "config 1")
+    y2 = ops.gemm(x, w, 20)
+    assert torch.equal(y, y2), "not deterministic"
+    del w
+
+
+def test_capi_nan_prefilled_output(capi, oracle):
+    """Through the C ABI with a NaN-filled output: every element must be written."""
+    lib = capi.lib()
+    ws = workspace(capi)
+    for M, K, N in [(8, 1024, 777), (3, 5120, 4096)]:
+        x, w = oracle.gen_f16(M, K, N, seed=N)
+        xd, wd = dev(x), dev(w)
+        y = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        rc = lib.b2_gemm_f16(xd.data_ptr(), wd.data_ptr(), y.data_ptr(), M, K, N, ws.data_ptr(),
+                             ws.numel(), stream_ptr())
+        capi.check(rc, "b2_gemm_f16")
+        check(y, oracle.gemm_ref(x, w), "capi")
+    torch.cuda.synchronize()
+    assert int(ws[:4].view(torch.int32).item()) == 0
+
+
+def test_deterministic_and_graph_replay(ops, oracle):
+    x, w = oracle.gen_f16(8, 4096, 6000, seed=77)
+    xd, wd = dev(x), dev(w)
+    y0 = ops.gemm(xd, wd, 20)
+    assert torch.equal(y0, ops.gemm(xd, wd, 20))
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            yg = ops.gemm(xd, wd, 20)
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(yg, y0)
+    # new activations through the same graph
+    x2, _ = oracle.gen_f16(8, 4096, 1, seed=78)
+    xd.copy_(dev(x2))
+    g.replay()
+    torch.cuda.synchronize()
+    check(yg, oracle.gemm_ref(x2, w), "graph replay")
+    assert ops.workspace_status(False) == 0
+
+
+def test_rejects_bad_inputs(ops):
+    x = torch.zeros(9, 64, dtype=torch.float16, device="cuda")
+    w = torch.zeros(128, 64, dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError):
+        ops.gemm(x, w, 0)  # M = 9
+    with pytest.raises(RuntimeError):
+        ops.gemm(x[:4].float(), w, 0)  # dtype
+    with pytest.raises(RuntimeError):
+        ops.gemm(torch.zeros(4, 60, dtype=torch.float16, device="cuda"),
+                 torch.zeros(128, 60, dtype=torch.float16, device="cuda"), 0)  # K % 8
+    with pytest.raises(RuntimeError):
+        ops.gemm(x[:4], w[:, :32], 0)  # K mismatch
