@@ -355,84 +355,132 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_sweep(args):
-    from oracle import cpu_baseline  # noqa: F401  (imported for symmetry; sweep is GPU-only)
+SWEEP = (
+    [("cfg1_lm_head", "f16", 7, 5120, 151936, 0), ("cfg0", "w4", 7, 4096, 4096, 128)]
+    + [(f"cfg2_{nm}_M{M}", "w4", M, K, N, 128) for M in (1, 2, 4, 8)
+       for nm, (K, N) in {"qkv": (5120, 8192), "o_proj": (6144, 5120), "gate_up": (5120, 34816),
+                          "down": (17408, 5120)}.items()]
+    + [(f"cfg3_down_TP{P}", "w4", 8, 17408 // P, 5120, 128) for P in (2, 4, 8)]
+    + [(f"drafter_fc_M{M}", "f16", M, 25600, 5120, 0) for M in (1, 8)]
+    + [("check_w4_G32", "w4", 8, 5120, 1024, 32)]
+)
 
+
+def run_sweep(args):
+    """Every BASELINE config on one GPU. Launches are captured in a CUDA graph that rotates over
+    enough weight copies to exceed 3x L2 (so every launch reads HBM), and timed by replaying the
+    graph: the time per launch excludes host launch overhead, as in a captured decode step."""
     import torch
 
     import __graft_entry__ as entry
 
-    pkg = entry.load_package()
+    entry.load_package()
     from mi50_vllm_lab_b200 import capi
 
     lib = capi.lib()
     torch.cuda.set_device(0)
     ws = torch.zeros(lib.b2_workspace_bytes(0), dtype=torch.uint8, device="cuda")
-    sp = torch.cuda.current_stream().cuda_stream
-    stream = torch.cuda.current_stream()
     peak, _ = hbm_peak()
     l2 = torch.cuda.get_device_properties(0).L2_cache_size
 
-    def bench_w4(name, M, K, N, G):
-        nb = w4_bytes(M, K, N, G)
-        copies = max(1, int(3 * l2 // (K * N // 2)) + 1)
+    def measure(name, kind, M, K, N, G):
+        wbytes = K * N // 2 if kind == "w4" else 2 * N * K
+        nb = w4_bytes(M, K, N, G) if kind == "w4" else f16_bytes(M, K, N)
+        copies = max(1, int(3 * l2 // wbytes) + 1)
         g = torch.Generator(device="cuda").manual_seed(M * K + N)
-        sets = []
+        x = torch.randn(M, K, device="cuda", generator=g).half()
+        y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+        calls = []
         for _ in range(copies):
-            qw = torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32, generator=g)
-            qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda", dtype=torch.int32, generator=g)
-            sc = (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half()
-            sets.append((qw, qz, sc))
-        x = torch.randn(M, K, device="cuda", generator=g).half()
-        y = torch.empty(M, N, dtype=torch.float16, device="cuda")
-        it = [0]
+            if kind == "w4":
+                qw = torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32, generator=g)
+                qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda", dtype=torch.int32, generator=g)
+                sc = (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half()
+                calls.append((qw, qz, sc))
+            else:
+                calls.append((torch.randn(N, K, device="cuda", generator=g) * 0.02).half(),)
 
-        def step():
-            qw, qz, sc = sets[it[0] % copies]
-            it[0] += 1
-            capi.check(lib.b2_w4_gemm(x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(),
-                                      y.data_ptr(), M, K, N, G, ws.data_ptr(), ws.numel(), sp))
-        for _ in range(max(args.warmup, copies)):
-            step()
-        _, per = time_steps(step, args.steps, 1, stream)
-        us = statistics.median(per) * 1e3
-        return {"workload": name, "M": M, "K": K, "N": N, "G": G, "us": round(us, 2),
+        def launch(t, sp):
+            if kind == "w4":
+                qw, qz, sc = t
+                rc = lib.b2_w4_gemm(x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(),
+                                    y.data_ptr(), M, K, N, G, ws.data_ptr(), ws.numel(), sp)
+            else:
+                rc = lib.b2_gemm_f16(x.data_ptr(), t[0].data_ptr(), y.data_ptr(), M, K, N,
+                                     ws.data_ptr(), ws.numel(), sp)
+            capi.check(rc, name)
+
+        reps = max(copies, min(64, 20 * copies))
+        reps = (reps // copies) * copies
+        sp0 = torch.cuda.current_stream().cuda_stream
+        for t in calls:
+            launch(t, sp0)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                for i in range(reps):
+                    launch(calls[i % copies], s.cuda_stream)
+        torch.cuda.current_stream().wait_stream(s)
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        times = []
+        for _ in range(max(3, args.steps // reps)):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            graph.replay()
+            e1.record(st)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e3 / reps)
+        us = statistics.median(times)
+        del graph
+        return {"workload": name, "kind": kind, "M": M, "K": K, "N": N, "G": G, "us": round(us, 2),
                 "TBps": round(nb / us / 1e6, 3), "frac": round(nb / us / 1e3 / peak, 3),
-                "l2_rotation_copies": copies}
+                "bytes": nb, "l2_rotation_copies": copies, "launches_per_graph": reps}
 
-    def bench_f16(name, M, K, N):
-        nb = f16_bytes(M, K, N)
-        copies = max(1, int(3 * l2 // (2 * N * K)) + 1)
-        g = torch.Generator(device="cuda").manual_seed(N)
-        ws_ = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).half() for _ in range(copies)]
-        x = torch.randn(M, K, device="cuda", generator=g).half()
-        y = torch.empty(M, N, dtype=torch.float16, device="cuda")
-        it = [0]
+    for w in SWEEP:
+        if args.only and args.only not in w[0]:
+            continue
+        print(json.dumps(measure(*w)), flush=True)
+        torch.cuda.empty_cache()
 
-        def step():
-            w = ws_[it[0] % copies]
-            it[0] += 1
-            capi.check(lib.b2_gemm_f16(x.data_ptr(), w.data_ptr(), y.data_ptr(), M, K, N,
-                                       ws.data_ptr(), ws.numel(), sp))
-        for _ in range(max(args.warmup, copies)):
-            step()
-        _, per = time_steps(step, args.steps, 1, stream)
-        us = statistics.median(per) * 1e3
-        return {"workload": name, "M": M, "K": K, "N": N, "us": round(us, 2),
-                "TBps": round(nb / us / 1e6, 3), "frac": round(nb / us / 1e3 / peak, 3),
-                "l2_rotation_copies": copies}
 
-    rows = [bench_f16("cfg1 lm_head", 7, 5120, 151936), bench_w4("cfg0", 7, 4096, 4096, 128)]
-    for M in (1, 2, 4, 8):
-        for nm, (K, N) in {"qkv": (5120, 8192), "o_proj": (6144, 5120), "gate_up": (5120, 34816),
-                           "down": (17408, 5120)}.items():
-            rows.append(bench_w4(f"cfg2 {nm}", M, K, N, 128))
-    for P in (2, 4, 8):
-        rows.append(bench_w4(f"cfg3 down shard TP{P}", 8, 17408 // P, 5120, 128))
-    for M in (1, 8):
-        rows.append(bench_f16("drafter fc", M, 25600, 5120))
-    for r in rows:
-        print(json.dumps(r), flush=True)
+def run_profile(args):
+    """A few eager launches of one sweep workload, for ncu: warm-up launches, then `steps`."""
+    import torch
+
+    import __graft_entry__ as entry
+
+    entry.load_package()
+    from mi50_vllm_lab_b200 import capi
+
+    lib = capi.lib()
+    torch.cuda.set_device(0)
+    ws = torch.zeros(lib.b2_workspace_bytes(0), dtype=torch.uint8, device="cuda")
+    name, kind, M, K, N, G = next(w for w in SWEEP if args.only in w[0])
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    sp = torch.cuda.current_stream().cuda_stream
+    if kind == "w4":
+        qw = torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32, generator=g)
+        qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda", dtype=torch.int32, generator=g)
+        sc = (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half()
+        step = lambda: capi.check(lib.b2_w4_gemm(x.data_ptr(), qw.data_ptr(), qz.data_ptr(),  # noqa: E731
+                                                 sc.data_ptr(), y.data_ptr(), M, K, N, G,
+                                                 ws.data_ptr(), ws.numel(), sp))
+    else:
+        w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+        step = lambda: capi.check(lib.b2_gemm_f16(x.data_ptr(), w.data_ptr(), y.data_ptr(), M, K,  # noqa: E731
+                                                  N, ws.data_ptr(), ws.numel(), sp))
+    for _ in range(args.warmup + args.steps):
+        step()
+    torch.cuda.synchronize()
+    print(json.dumps({"profiled": name, "launches": args.warmup + args.steps}))
 
 
 def main():
@@ -442,6 +490,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--sweep", action="store_true")
+    ap.add_argument("--only", default="", help="with --sweep/--profile: workloads whose name contains this")
+    ap.add_argument("--profile", action="store_true", help="eager launches of one --only workload (for ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     args = ap.parse_args()
@@ -449,9 +499,9 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.profile:
+        run_profile(args)
     elif args.sweep:
-        if args.steps > 500:
-            args.steps = 200
         run_sweep(args)
     else:
         run_gpu(args)

@@ -169,4 +169,29 @@ __host__ __device__ __forceinline__ int sk_slot(const StreamK& s, int cta, int t
   return (sk_begin(s, cta) / s.upt == tile) ? 0 : 1;
 }
 
+// The same rule without division, for the hot paths: a CTA whose range starts at unit `begin`
+// uses slot 0 for the tile starting at unit `tile_start` iff it starts inside that tile. Of a
+// tile's contributors first..last only `first` can start before the tile, so the reducer needs
+// one sk_begin (for `first`) per tile instead of one per contributor.
+__device__ __forceinline__ int sk_slot_from_begin(long long begin, long long tile_start) {
+  return begin >= tile_start ? 0 : 1;
+}
+
+// Walks a CTA's unit range as (tile, k-unit) pairs without dividing in the loop.
+struct UnitCursor {
+  int tile, ku, left;
+  __device__ __forceinline__ UnitCursor(const StreamK& s, long long lo, long long hi) {
+    tile = (int)(lo / s.upt);
+    ku = (int)(lo - (long long)tile * s.upt);
+    left = (int)(hi - lo);
+  }
+  __device__ __forceinline__ bool segment_end(const StreamK& s) const {
+    return ku == s.upt - 1 || left == 1;
+  }
+  __device__ __forceinline__ void next(const StreamK& s) {
+    --left;
+    if (++ku == s.upt) ku = 0, ++tile;
+  }
+};
+
 }  // namespace b2

@@ -28,6 +28,7 @@ constexpr int kUnitK = 64;                               // k per unit = one 128
 constexpr int kStageBytes = kTileN * kUnitK * 2;         // 16 KB
 constexpr int kStages = 6;
 constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 2 * kStages * 8 + 16;
+static_assert(kStageBytes % 1024 == 0, "swizzled TMA boxes start on 1024-byte boundaries");
 
 struct F16Args {
   const __half* x;
@@ -87,11 +88,11 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
       bool used[kStages];
 #pragma unroll
       for (int s = 0; s < kStages; ++s) used[s] = false, last_ph[s] = 0;
-      for (long long u = u_lo; u < u_hi; ++u) {
+      for (UnitCursor cu(sk, u_lo, u_hi); cu.left > 0; cu.next(sk)) {
         if (!mbar_wait(&empty[st], ph ^ 1u, s_abort)) break;
-        const int tile = (int)(u / sk.upt), ku = (int)(u % sk.upt);
         mbar_arrive_expect_tx(&full[st], kStageBytes);
-        tma_load_2d(smem + st * kStageBytes, &tm_w, &full[st], ku * kUnitK, tile * kTileN, pol);
+        tma_load_2d(smem + st * kStageBytes, &tm_w, &full[st], cu.ku * kUnitK, cu.tile * kTileN,
+                    pol);
         used[st] = true;
         last_ph[st] = ph;
         if (++st == kStages) st = 0, ph ^= 1u;
@@ -123,8 +124,8 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
   int st = 0;
   uint32_t ph = 0;
   bool ok = true;
-  for (long long u = u_lo; u < u_hi; ++u) {
-    const int tile = (int)(u / sk.upt), ku = (int)(u % sk.upt);
+  for (UnitCursor cu(sk, u_lo, u_hi); cu.left > 0; cu.next(sk)) {
+    const int tile = cu.tile, ku = cu.ku;
     uint4 xv[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -149,7 +150,7 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
     if (lane == 0) mbar_arrive(&empty[st]);
     if (++st == kStages) st = 0, ph ^= 1u;
 
-    if (ku != sk.upt - 1 && u != u_hi - 1) continue;
+    if (!cu.segment_end(sk)) continue;
     // ---------------------------------------------------------------- end of a tile segment
     float v[2][4];
 #pragma unroll
@@ -165,7 +166,8 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
       store_out(p, tile, warp, g, t, v);
       continue;
     }
-    float* slot = p.partials + ((size_t)blockIdx.x * 2 + sk_slot(sk, blockIdx.x, tile)) * kSlotFloats;
+    float* slot =
+        p.partials + ((size_t)blockIdx.x * 2 + sk_slot_from_begin(u_lo, ts)) * kSlotFloats;
 #pragma unroll
     for (int T = 0; T < 2; ++T)
 #pragma unroll
@@ -174,32 +176,49 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
         const int r = warp * 32 + T * 16 + g + (i >> 1) * 8;
         if (m < p.M) __stcg(&slot[m * kTileN + r], v[T][i]);
       }
-    __threadfence();
+    // one release by one thread after the barrier covers the whole CTA's stores
     named_bar_sync(1, kWarps * 32);
     if (threadIdx.x == 0) {
+      __threadfence();
       const int prev = atomicAdd(&p.counters[tile], 1);
       const int fin = (prev == last - first);
-      if (fin) atomicExch(&p.counters[tile], 0);
+      if (fin) {
+        atomicExch(&p.counters[tile], 0);
+        __threadfence();
+      }
       *s_flag = fin;
     }
     named_bar_sync(1, kWarps * 32);
     if (!*s_flag) continue;
-    __threadfence();
+    // add the contributors' slots in CTA order, two contributors' loads in flight at a time
     float s[2][4];
 #pragma unroll
     for (int T = 0; T < 2; ++T)
 #pragma unroll
       for (int i = 0; i < 4; ++i) s[T][i] = 0.f;
-    for (int c = first; c <= last; ++c) {
-      const float* sl = p.partials + ((size_t)c * 2 + sk_slot(sk, c, tile)) * kSlotFloats;
+    const int first_slot = sk_slot_from_begin(sk_begin(sk, first), ts);
+    for (int c0 = first; c0 <= last; c0 += 2) {
+      float a[2][2][4];
 #pragma unroll
-      for (int T = 0; T < 2; ++T)
+      for (int b = 0; b < 2; ++b) {
+        const int c = c0 + b;
+        const float* sl = p.partials + ((size_t)c * 2 + (c == first ? first_slot : 0)) * kSlotFloats;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int m = 2 * t + (i & 1);
-          const int r = warp * 32 + T * 16 + g + (i >> 1) * 8;
-          if (m < p.M) s[T][i] += __ldcg(&sl[m * kTileN + r]);
-        }
+        for (int T = 0; T < 2; ++T)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int m = 2 * t + (i & 1);
+            const int r = warp * 32 + T * 16 + g + (i >> 1) * 8;
+            a[b][T][i] = (c <= last && m < p.M) ? __ldcg(&sl[m * kTileN + r]) : 0.f;
+          }
+      }
+#pragma unroll
+      for (int b = 0; b < 2; ++b)
+        if (c0 + b <= last)
+#pragma unroll
+          for (int T = 0; T < 2; ++T)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) s[T][i] += a[b][T][i];
     }
     store_out(p, tile, warp, g, t, s);
   }

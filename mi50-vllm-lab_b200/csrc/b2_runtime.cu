@@ -73,9 +73,68 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
+// Encoding a tensor map costs microseconds of host time, comparable to a whole small GEMM, so
+// maps are kept in a small per-thread cache keyed by everything they encode. A map depends only
+// on these values, so a hit is always valid (even if the memory was freed and reallocated).
+namespace {
+struct MapKey {
+  const void* base;
+  uint64_t inner, outer, stride;
+  uint32_t box_inner, box_outer;
+  int dtype, swizzle, device;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && inner == o.inner && outer == o.outer && stride == o.stride &&
+           box_inner == o.box_inner && box_outer == o.box_outer && dtype == o.dtype &&
+           swizzle == o.swizzle && device == o.device;
+  }
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  bool valid;
+};
+constexpr int kMapCache = 64;
+thread_local MapEntry t_maps[kMapCache];
+
+size_t map_hash(const MapKey& k) {
+  size_t h = reinterpret_cast<uintptr_t>(k.base) >> 4;
+  h = h * 1000003u ^ (size_t)k.inner;
+  h = h * 1000003u ^ (size_t)k.outer;
+  h = h * 1000003u ^ ((size_t)k.box_inner << 8 | k.box_outer);
+  h = h * 1000003u ^ (size_t)(k.dtype * 31 + k.swizzle * 7 + k.device);
+  return h;
+}
+}  // namespace
+
+int encode_2d_uncached(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                       uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                       uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
               uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
               CUtensorMapSwizzle swizzle) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const MapKey key{base, inner, outer, row_stride_bytes, box_inner, box_outer, (int)dtype,
+                   (int)swizzle, dev};
+  MapEntry& e = t_maps[map_hash(key) % kMapCache];
+  if (e.valid && e.key == key) {
+    *map = e.map;
+    return B2_OK;
+  }
+  const int rc = encode_2d_uncached(map, dtype, base, inner, outer, row_stride_bytes, box_inner,
+                                    box_outer, swizzle);
+  if (rc == B2_OK) {
+    e.key = key;
+    e.map = *map;
+    e.valid = true;
+  }
+  return rc;
+}
+
+int encode_2d_uncached(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
+                       uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                       uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   auto fn = get_encode_fn();
   if (!fn) return fail(B2_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   cuuint64_t dims[2] = {inner, outer};

@@ -37,16 +37,30 @@ constexpr int kThreads = (kWarps + 1) * 32;
 constexpr int kUnitK = 128;                 // k per unit = 16 word rows
 constexpr int kQwBox = 16 * 128;            // 16 word rows x 32 columns x 4 B (one TMA box)
 constexpr int kQwStage = kWarps * kQwBox;   // 8 KB
-constexpr int kStages = 8;
 
+constexpr int align128(int v) { return (v + 127) & ~127; }
+
+// Shared memory of one CTA (offsets from a 1024-byte aligned base). Every TMA destination must
+// start on a 128-byte boundary, and the swizzled qw boxes on a 1024-byte one.
 template <int GP>  // GP: 32-k pairs per scale group inside a unit (1: G=32, 2: G=64, 4: G>=128)
 struct Cfg {
+  // Stages per CTA: 6 x 8.5 KB lets four CTAs (16 consumer warps) share an SM's 228 KB when
+  // G >= 128 (the exact-dequant variants need more registers and run three CTAs per SM).
+  static constexpr int kStages = 6;
   static constexpr int RG = 4 / GP;                        // group rows per unit
   static constexpr int kScBytes = RG * kTileN * 2;         // scales of one unit
   static constexpr int kQzBytes = RG * (kTileN / 8) * 4;   // zeros of one unit
+  static constexpr int kScStride = align128(kScBytes);
+  static constexpr int kQzStride = align128(kQzBytes);
   static constexpr int kTx = kQwStage + kScBytes + kQzBytes;
-  static constexpr int kSmem =
-      1024 + kStages * (kQwStage + kScBytes + kQzBytes) + 2 * kStages * 8 + 32;
+  static constexpr int kScOff = kStages * kQwStage;
+  static constexpr int kQzOff = kScOff + kStages * kScStride;
+  static constexpr int kBarOff = kQzOff + kStages * kQzStride;
+  static constexpr int kSmem = 1024 + kBarOff + 2 * kStages * 8 + 32;
+  static_assert(kQwBox % 1024 == 0 && kQwStage % 1024 == 0, "swizzled boxes need 1024 B");
+  static_assert(kScOff % 128 == 0 && kScStride % 128 == 0, "TMA destination alignment");
+  static_assert(kQzOff % 128 == 0 && kQzStride % 128 == 0, "TMA destination alignment");
+  static_assert(kBarOff % 8 == 0, "mbarrier alignment");
 };
 
 struct W4Args {
@@ -114,21 +128,55 @@ __device__ __forceinline__ void store_y(const W4Args& p, int tile, int colw, int
   }
 }
 
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// The eight nibbles of one word as 1024 + q (low nibble of a byte, k = 0,1 and 4,5 of the word)
+// or 1024 + 16q (high nibble, k = 2,3 and 6,7), exact fp16, without subtracting anything: four
+// lop3 and one shift. The offsets are removed after the dot product (see the kernel comment).
+__device__ __forceinline__ void magic_word(uint32_t q, uint32_t (&d)[4]) {
+  constexpr uint32_t kMagic = 0x64006400u;
+  const uint32_t q8 = q >> 8;
+  d[0] = lop_and_or(q, 0x000F000Fu, kMagic);
+  d[1] = lop_and_or(q, 0x00F000F0u, kMagic);
+  d[2] = lop_and_or(q8, 0x000F000Fu, kMagic);
+  d[3] = lop_and_or(q8, 0x00F000F0u, kMagic);
+}
+
+// float(z) for 0 <= z < 2^23 without the conversion unit
+__device__ __forceinline__ float small_uint_to_float(uint32_t z) {
+  return __int_as_float(0x4B000000 | z) - 8388608.0f;
+}
+
+// Two ways to turn a word into the mma A operand, chosen by the group size:
+//  * EXACT (G = 32, 64): A = (q - z) in fp16 (lop3 + add/fma.f16x2, exact); the fp32 sum of a
+//    group is scaled once: acc += s * sum.
+//  * OFFSET (G >= 128): A = 1024 + q or 1024 + 16q (lop3 only) and B = x or x/16 (the activation
+//    pairs of high nibbles pre-scaled by 1/16, exact), so the dot product of a group is
+//        P = sum_k q_k x_k + C,   C = 1024 * sum_{low k} x + 64 * sum_{high k} x.
+//    Two more mma per 32 k with constant A rows (1024 | 1024 gives C; 1 | 16 gives S = sum x)
+//    produce C and S in fp32, and the fold is acc += s * (P - C - z * S). This removes the four
+//    fp16 subtractions per word from the inner loop; the price is that P and C carry an offset of
+//    ~1024 * |sum x| that cancels in fp32 (about 1e-4 of |y| at these sizes, below the fp16
+//    rounding of the output).
 template <int GP, bool FUSED>
-__global__ void __launch_bounds__(kThreads) w4_kernel(const __grid_constant__ CUtensorMap tm_qw,
-                                                      const __grid_constant__ CUtensorMap tm_sc,
-                                                      const __grid_constant__ CUtensorMap tm_qz,
-                                                      const W4Args p, const ArView ar) {
+__global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
+    w4_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_sc,
+              const __grid_constant__ CUtensorMap tm_qz, const W4Args p, const ArView ar) {
   using C = Cfg<GP>;
   constexpr int RG = C::RG;
+  constexpr int kStages = C::kStages;
+  constexpr bool OFFSET = (GP == 4);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* s_qw = smem;
-  __half* s_sc = reinterpret_cast<__half*>(smem + kStages * kQwStage);
-  uint32_t* s_qz = reinterpret_cast<uint32_t*>(smem + kStages * (kQwStage + C::kScBytes));
-  uint64_t* full =
-      reinterpret_cast<uint64_t*>(smem + kStages * (kQwStage + C::kScBytes + C::kQzBytes));
+  uint8_t* s_sc = smem + C::kScOff;  // stage st at s_sc + st * kScStride: [RG][128] fp16
+  uint8_t* s_qz = smem + C::kQzOff;  // stage st at s_qz + st * kQzStride: [RG][16] int32
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* empty = full + kStages;
   volatile int* s_abort = reinterpret_cast<volatile int*>(empty + kStages);
   volatile int* s_flag = s_abort + 1;
@@ -163,18 +211,18 @@ __global__ void __launch_bounds__(kThreads) w4_kernel(const __grid_constant__ CU
       bool used[kStages];
 #pragma unroll
       for (int s = 0; s < kStages; ++s) used[s] = false, last_ph[s] = 0;
-      for (long long u = u_lo; u < u_hi; ++u) {
+      for (UnitCursor cu(sk, u_lo, u_hi); cu.left > 0; cu.next(sk)) {
         if (!mbar_wait(&empty[st], ph ^ 1u, s_abort)) break;
-        const int tile = (int)(u / sk.upt), ku = (int)(u % sk.upt);
-        const int n0 = tile * kTileN;
+        const int ku = cu.ku;
+        const int n0 = cu.tile * kTileN;
         const int grow = (ku * kUnitK) / p.G;
         mbar_arrive_expect_tx(&full[st], C::kTx);
 #pragma unroll
         for (int w = 0; w < kWarps; ++w)
           tma_load_2d(s_qw + st * kQwStage + w * kQwBox, &tm_qw, &full[st], n0 + 32 * w, ku * 16,
                       pol);
-        tma_load_2d(s_sc + st * (RG * kTileN), &tm_sc, &full[st], n0, grow, pol);
-        tma_load_2d(s_qz + st * (RG * kTileN / 8), &tm_qz, &full[st], n0 / 8, grow, pol);
+        tma_load_2d(s_sc + st * C::kScStride, &tm_sc, &full[st], n0, grow, pol);
+        tma_load_2d(s_qz + st * C::kQzStride, &tm_qz, &full[st], n0 / 8, grow, pol);
         used[st] = true;
         last_ph[st] = ph;
         if (++st == kStages) st = 0, ph ^= 1u;
@@ -197,31 +245,58 @@ __global__ void __launch_bounds__(kThreads) w4_kernel(const __grid_constant__ CU
   const bool has_row = g < p.M;
   const __half* xrow = p.x + (size_t)(has_row ? g : 0) * p.K;
   const uint32_t e = FUSED ? *s_gen : 0u;
+  // constant A rows of the correction mma (OFFSET): row 0 = 1024 everywhere (C), row 1 = 1 on
+  // low-nibble k and 16 on high-nibble k (S); rows 2..15 zero
+  const uint32_t cs_lo = g == 0 ? 0x64006400u : (g == 1 ? 0x3C003C00u : 0u);
+  const uint32_t cs_hi = g == 0 ? 0x64006400u : (g == 1 ? 0x4C004C00u : 0u);
 
-  float acc[2][4], accg[2][4];
+  float acc[2][4], accg[2][4], acs[4];
 #pragma unroll
   for (int T = 0; T < 2; ++T)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[T][i] = accg[T][i] = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acs[i] = 0.f;
+
+  auto load_x = [&](int ku_, uint4 (&dst)[4]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      dst[q] = has_row ? ldg_nc128(xrow + ku_ * kUnitK + 32 * q + 8 * t) : make_uint4(0, 0, 0, 0);
+  };
+  uint4 xn[4];
+  {
+    UnitCursor c0(sk, u_lo, u_hi);
+    load_x(c0.ku, xn);
+  }
 
   int st = 0;
   uint32_t ph = 0;
   bool ok = true;
-  for (long long u = u_lo; u < u_hi; ++u) {
-    const int tile = (int)(u / sk.upt), ku = (int)(u % sk.upt);
+  for (UnitCursor cu(sk, u_lo, u_hi); cu.left > 0; cu.next(sk)) {
+    const int tile = cu.tile, ku = cu.ku;
     uint4 xv[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q)
-      xv[q] = has_row ? ldg_nc128(xrow + ku * kUnitK + 32 * q + 8 * t) : make_uint4(0, 0, 0, 0);
+    for (int q = 0; q < 4; ++q) xv[q] = xn[q];
+    if (cu.left > 1) load_x(ku + 1 == sk.upt ? 0 : ku + 1, xn);  // next unit's activations
+    if (OFFSET) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {  // high-nibble pairs (k 2,3 and 6,7 of each 8) times 1/16
+        xv[q].y = hmul2_u(xv[q].y, 0x2C002C00u);
+        xv[q].w = hmul2_u(xv[q].w, 0x2C002C00u);
+      }
+    }
     if (ok) ok = mbar_wait(&full[st], ph, s_abort);
 
-    // zero constants and scales of the lane's 4 columns for each group row of the unit
+    // zero points and scales of the lane's 4 columns for each group row of the unit
     uint32_t zlo[RG][4], zhi[RG][4];
-    float scl[RG][4];
+    float scl[RG][4], zf[RG][4];
 #pragma unroll
     for (int r = 0; r < RG; ++r) {
-      const uint32_t zw = s_qz[(st * RG + r) * (kTileN / 8) + (colw >> 3)] >> ((colw & 7) * 4);
-      const uint2 sv = *reinterpret_cast<const uint2*>(s_sc + (st * RG + r) * kTileN + colw);
+      const uint32_t* qz_row =
+          reinterpret_cast<const uint32_t*>(s_qz + st * C::kQzStride) + r * (kTileN / 8);
+      const __half* sc_row = reinterpret_cast<const __half*>(s_sc + st * C::kScStride) + r * kTileN;
+      const uint32_t zw = qz_row[colw >> 3] >> ((colw & 7) * 4);
+      const uint2 sv = *reinterpret_cast<const uint2*>(sc_row + colw);
       const __half2 s01 = *reinterpret_cast<const __half2*>(&sv.x);
       const __half2 s23 = *reinterpret_cast<const __half2*>(&sv.y);
       scl[r][0] = __low2float(s01);
@@ -231,8 +306,12 @@ __global__ void __launch_bounds__(kThreads) w4_kernel(const __grid_constant__ CU
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint32_t z = (zw >> (4 * i)) & 0xFu;
-        zlo[r][i] = (0xE400u + z) * 0x00010001u;         // -(1024 + z)
-        zhi[r][i] = (0xD400u + (z << 4)) * 0x00010001u;  // -(64 + z)
+        if (OFFSET) {
+          zf[r][i] = small_uint_to_float(z);
+        } else {
+          zlo[r][i] = (0xE400u + z) * 0x00010001u;         // -(1024 + z)
+          zhi[r][i] = (0xD400u + (z << 4)) * 0x00010001u;  // -(64 + z)
+        }
       }
     }
 
@@ -243,16 +322,27 @@ __global__ void __launch_bounds__(kThreads) w4_kernel(const __grid_constant__ CU
       const uint4 w = lds128(qb + row * 128 + ((ch ^ (row & 7)) << 4));
       const int r = (RG == 1) ? 0 : (q / GP);
       uint32_t d0[4], d1[4], d2[4], d3[4];
-      dequant_word(w.x, zlo[r][0], zhi[r][0], d0);
-      dequant_word(w.y, zlo[r][1], zhi[r][1], d1);
-      dequant_word(w.z, zlo[r][2], zhi[r][2], d2);
-      dequant_word(w.w, zlo[r][3], zhi[r][3], d3);
+      if (OFFSET) {
+        magic_word(w.x, d0);
+        magic_word(w.y, d1);
+        magic_word(w.z, d2);
+        magic_word(w.w, d3);
+      } else {
+        dequant_word(w.x, zlo[r][0], zhi[r][0], d0);
+        dequant_word(w.y, zlo[r][1], zhi[r][1], d1);
+        dequant_word(w.z, zlo[r][2], zhi[r][2], d2);
+        dequant_word(w.w, zlo[r][3], zhi[r][3], d3);
+      }
       // n-tile 0: A rows g / g+8 = columns colw / colw+1; n-tile 1: colw+2 / colw+3
       mma_16816(accg[0], d0[0], d1[0], d0[1], d1[1], xv[q].x, xv[q].y);
       mma_16816(accg[0], d0[2], d1[2], d0[3], d1[3], xv[q].z, xv[q].w);
       mma_16816(accg[1], d2[0], d3[0], d2[1], d3[1], xv[q].x, xv[q].y);
       mma_16816(accg[1], d2[2], d3[2], d2[3], d3[3], xv[q].z, xv[q].w);
-      if ((q + 1) % GP == 0) {
+      if (OFFSET) {
+        mma_16816(acs, cs_lo, 0u, cs_hi, 0u, xv[q].x, xv[q].y);
+        mma_16816(acs, cs_lo, 0u, cs_hi, 0u, xv[q].z, xv[q].w);
+      }
+      if (!OFFSET && (q + 1) % GP == 0) {
 #pragma unroll
         for (int T = 0; T < 2; ++T)
 #pragma unroll
@@ -262,11 +352,30 @@ __global__ void __launch_bounds__(kThreads) w4_kernel(const __grid_constant__ CU
           }
       }
     }
+    if (OFFSET) {
+      // C[m], S[m] for this lane's rows m = 2t, 2t+1 live in lanes t (row 0) and 4+t (row 1)
+      const float c0 = __shfl_sync(0xffffffffu, acs[0], t);
+      const float c1 = __shfl_sync(0xffffffffu, acs[1], t);
+      const float s0 = __shfl_sync(0xffffffffu, acs[0], 4 + t);
+      const float s1 = __shfl_sync(0xffffffffu, acs[1], 4 + t);
+#pragma unroll
+      for (int T = 0; T < 2; ++T)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int col = 2 * T + (i >> 1);
+          const float cm = (i & 1) ? c1 : c0, sm = (i & 1) ? s1 : s0;
+          const float d = fmaf(-zf[0][col], sm, accg[T][i] - cm);
+          acc[T][i] = fmaf(scl[0][col], d, acc[T][i]);
+          accg[T][i] = 0.f;
+        }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acs[i] = 0.f;
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     if (++st == kStages) st = 0, ph ^= 1u;
 
-    if (ku != sk.upt - 1 && u != u_hi - 1) continue;
+    if (!cu.segment_end(sk)) continue;
     // ---------------------------------------------------------------- end of a tile segment
     float4 v[2];
     v[0] = make_float4(acc[0][0], acc[0][2], acc[1][0], acc[1][2]);  // m = 2t
@@ -281,35 +390,52 @@ __global__ void __launch_bounds__(kThreads) w4_kernel(const __grid_constant__ CU
     bool finisher = true;
     if (first != last) {
       float* slot =
-          p.partials + ((size_t)blockIdx.x * 2 + sk_slot(sk, blockIdx.x, tile)) * kSlotFloats;
+          p.partials + ((size_t)blockIdx.x * 2 + sk_slot_from_begin(u_lo, ts)) * kSlotFloats;
 #pragma unroll
       for (int j = 0; j < 2; ++j)
         if (2 * t + j < p.M)
           __stcg(reinterpret_cast<float4*>(slot + (2 * t + j) * kTileN + colw), v[j]);
-      __threadfence();
+      // one release by one thread after the barrier covers the whole CTA's stores
       named_bar_sync(1, kWarps * 32);
       if (threadIdx.x == 0) {
+        __threadfence();
         const int prev = atomicAdd(&p.counters[tile], 1);
         const int fin = (prev == last - first);
-        if (fin) atomicExch(&p.counters[tile], 0);
+        if (fin) {
+          atomicExch(&p.counters[tile], 0);
+          __threadfence();
+        }
         *s_flag = fin;
       }
       named_bar_sync(1, kWarps * 32);
       finisher = *s_flag != 0;
       if (finisher) {
-        __threadfence();
+        // add the contributors' slots in CTA order, four loads in flight at a time
         v[0] = v[1] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = first; c <= last; ++c) {
-          const float* sl = p.partials + ((size_t)c * 2 + sk_slot(sk, c, tile)) * kSlotFloats;
+        const int first_slot = sk_slot_from_begin(sk_begin(sk, first), ts);
+        for (int c0 = first; c0 <= last; c0 += 4) {
+          float4 a[4][2];
 #pragma unroll
-          for (int j = 0; j < 2; ++j)
-            if (2 * t + j < p.M) {
-              const float4 a = __ldcg(reinterpret_cast<const float4*>(sl + (2 * t + j) * kTileN + colw));
-              v[j].x += a.x;
-              v[j].y += a.y;
-              v[j].z += a.z;
-              v[j].w += a.w;
-            }
+          for (int b = 0; b < 4; ++b) {
+            const int c = c0 + b;
+            const float* sl =
+                p.partials + ((size_t)c * 2 + (c == first ? first_slot : 0)) * kSlotFloats;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              a[b][j] = (c <= last && 2 * t + j < p.M)
+                            ? __ldcg(reinterpret_cast<const float4*>(sl + (2 * t + j) * kTileN + colw))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int b = 0; b < 4; ++b)
+            if (c0 + b <= last)
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                v[j].x += a[b][j].x;
+                v[j].y += a[b][j].y;
+                v[j].z += a[b][j].z;
+                v[j].w += a[b][j].w;
+              }
         }
       }
     }
@@ -334,35 +460,36 @@ __global__ void __launch_bounds__(kThreads) w4_kernel(const __grid_constant__ CU
     if (threadIdx.x == 0) ar_publish(ar, tile, e);
   }
   if (!ok && lane == 0) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
-  if (!FUSED) return;
-
-  // ------------------------------------------------------------------ fused all-reduce, phase 2
-  // CTA b adds tiles b, b + grid, ... over all ranks in rank order and writes the fp16 result.
-  for (int tile = blockIdx.x; tile < sk.tiles; tile += gridDim.x) {
-    named_bar_sync(1, kWarps * 32);
-    if (threadIdx.x == 0) *s_flag = ar_wait(ar, tile, e) ? 1 : 0;
-    named_bar_sync(1, kWarps * 32);
-    __threadfence();
-    const int n = tile * kTileN + colw;
-    if (n >= p.N) continue;
-    float4 v[2];
-    v[0] = v[1] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int src = 0; src < ar.world; ++src) {
-      const float* sl = reinterpret_cast<const float*>(ar_slot(ar, ar.rank, e & 1u, src));
+  if constexpr (FUSED) {
+    // -------------------------------------------------------------- fused all-reduce, phase 2
+    // CTA b adds tiles b, b + grid, ... over all ranks in rank order and writes the fp16 result.
+    for (int tile = blockIdx.x; tile < sk.tiles; tile += gridDim.x) {
+      named_bar_sync(1, kWarps * 32);
+      if (threadIdx.x == 0) *s_flag = ar_wait(ar, tile, e) ? 1 : 0;
+      named_bar_sync(1, kWarps * 32);
+      __threadfence();
+      const int n = tile * kTileN + colw;
+      if (n >= p.N) continue;
+      float4 v[2];
+      v[0] = v[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int src = 0; src < ar.world; ++src) {
+        const float* sl = reinterpret_cast<const float*>(ar_slot(ar, ar.rank, e & 1u, src));
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
-        if (2 * t + j < p.M) {
-          const float4 a = __ldcg(reinterpret_cast<const float4*>(sl + (size_t)(2 * t + j) * p.N + n));
-          v[j].x += a.x;
-          v[j].y += a.y;
-          v[j].z += a.z;
-          v[j].w += a.w;
-        }
+        for (int j = 0; j < 2; ++j)
+          if (2 * t + j < p.M) {
+            const float4 a =
+                __ldcg(reinterpret_cast<const float4*>(sl + (size_t)(2 * t + j) * p.N + n));
+            v[j].x += a.x;
+            v[j].y += a.y;
+            v[j].z += a.z;
+            v[j].w += a.w;
+          }
+      }
+      store_y(p, tile, colw, t, v);
     }
-    store_y(p, tile, colw, t, v);
+    named_bar_sync(1, kWarps * 32);
+    if (threadIdx.x == 0) ar_finish(ar, e);
   }
-  named_bar_sync(1, kWarps * 32);
-  if (threadIdx.x == 0) ar_finish(ar, e);
 }
 
 struct KernelCache {
