@@ -107,6 +107,31 @@ int b2_w4_gemm(const void* a, const void* qw, const void* qz, const void* sc, vo
                int K, int N, int group_size, void* ws, size_t ws_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * W4A16 skinny GEMM that allocates nothing (no counterpart in the reference)
+ *
+ * Same operands, layouts, contract and results as b2_w4_gemm, but without the workspace
+ * argument: its split-K scratch is a fixed 2,113,792-byte array in device memory that the
+ * library reserves on every GPU it is loaded on and keeps until the process exits. It is for
+ * callers that cannot allocate device memory at the point of the call: hosts whose device
+ * memory belongs to a pool or allocator they cannot reach from where they call this (an FFI or
+ * JNI binding, an embedded runtime), code that must not risk the device-wide synchronisation or
+ * failure of a cudaMalloc in the middle of a decode step, and code that cannot keep a
+ * workspace alive between calls. This entry point calls no cudaMalloc, cudaFree or other
+ * allocating routine.
+ *   - Limit: N <= 524288 (4096 output tiles of 128 columns); larger N is rejected with
+ *     B2_ERR_INVALID_ARG. The split-K grid is capped at 256 CTAs.
+ *   - The first call on a device looks up the array's device address and zero-fills it, with a
+ *     synchronous cudaMemset; make that first call before any CUDA graph capture.
+ *   - Every call clears the array's counters on `stream` (cudaMemsetAsync) before its kernel.
+ *   - All calls on a device share the one array: calls that can overlap on the GPU (different
+ *     streams, or graphs replayed concurrently) race and give wrong results. Issue them in order.
+ *   - A device-side wait that gives up is recorded only in the array, which no entry point
+ *     reads; use b2_w4_gemm with b2_workspace_status where that report is needed.
+ * ---------------------------------------------------------------------------------------- */
+int b2_w4_gemm_noalloc(const void* a, const void* qw, const void* qz, const void* sc, void* y,
+                       int M, int K, int N, int group_size, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * Host-side rendezvous registry (POSIX shared memory, no GPU needed)
  *
  * Ranks of one node publish fixed-size blobs (CUDA IPC handles) under a shared-memory name and

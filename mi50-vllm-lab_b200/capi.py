@@ -39,6 +39,7 @@ _SIGS = {
     "b2_workspace_status": (_i, [_vp, _i, C.POINTER(_i)]),
     "b2_gemm_f16": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     "b2_w4_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "b2_w4_gemm_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "b2_registry_open": (_i, [C.c_char_p, _i, _i, C.POINTER(_vp)]),
     "b2_registry_put": (_i, [_vp, _i, _vp]),
     "b2_registry_get": (_i, [_vp, _i, _vp]),

@@ -22,6 +22,9 @@
 //     order (bit-identical on every rank).
 #include <cuda_fp16.h>
 
+#include <algorithm>
+#include <mutex>
+
 #include "b2_device.cuh"
 #include "b2_internal.h"
 #include "b2_nvar.cuh"
@@ -500,7 +503,7 @@ KernelCache g_cache[64][3][2];
 
 template <int GP, bool FUSED>
 int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, const ArView* ar,
-           cudaStream_t stream) {
+           int max_ctas, cudaStream_t stream) {
   using C = Cfg<GP>;
   W4Args a = a0;
   DeviceInfo di;
@@ -521,7 +524,7 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
   sk.upt = K / kUnitK;
   sk.tiles = (N + kTileN - 1) / kTileN;
   sk.total = (long long)sk.tiles * sk.upt;
-  sk.ctas = streamk_ctas(sk.total, di.sm_count, kc.occ, 4);
+  sk.ctas = std::min(streamk_ctas(sk.total, di.sm_count, kc.occ, 4), max_ctas);
   if (FUSED) {
     // Every CTA must be resident at once: a CTA waiting for peers must not hold back another
     // CTA of the same launch.
@@ -546,7 +549,20 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
 }
 
 int validate(const void* a, const void* qw, const void* qz, const void* sc, const void* y, int M,
+             int K, int N, int G);
+
+int validate(const void* a, const void* qw, const void* qz, const void* sc, const void* y, int M,
              int K, int N, int G, const void* ws, size_t ws_bytes) {
+  const int rc = validate(a, qw, qz, sc, y, M, K, N, G);
+  if (rc) return rc;
+  if (!ws || ws_bytes < ws_total_bytes())
+    return fail(B2_ERR_WORKSPACE, "w4: workspace of %zu B, need %zu B", ws_bytes, ws_total_bytes());
+  return B2_OK;
+}
+
+// Operand checks shared by every W4 entry point.
+int validate(const void* a, const void* qw, const void* qz, const void* sc, const void* y, int M,
+             int K, int N, int G) {
   if (!a || !qw || !qz || !sc || !y) return fail(B2_ERR_INVALID_ARG, "w4: null pointer");
   if (M < 1 || M > kMaxM) return fail(B2_ERR_INVALID_ARG, "w4: M=%d outside 1..8", M);
   if (K < kUnitK || K % kUnitK != 0)
@@ -561,8 +577,6 @@ int validate(const void* a, const void* qw, const void* qz, const void* sc, cons
   if ((reinterpret_cast<uintptr_t>(y) & 7u) != 0)
     return fail(B2_ERR_INVALID_ARG, "w4: y must be 8-byte aligned");
   if ((N + kTileN - 1) / kTileN > kWsMaxTiles) return fail(B2_ERR_INVALID_ARG, "w4: N=%d too large", N);
-  if (!ws || ws_bytes < ws_total_bytes())
-    return fail(B2_ERR_WORKSPACE, "w4: workspace of %zu B, need %zu B", ws_bytes, ws_total_bytes());
   return B2_OK;
 }
 
@@ -583,12 +597,55 @@ W4Args make_args(const void* a, void* y, int M, int K, int N, int G, void* ws) {
 
 template <bool FUSED>
 int dispatch(const W4Args& args, const void* qw, const void* qz, const void* sc, const ArView* ar,
-             cudaStream_t stream) {
+             cudaStream_t stream, int max_ctas = kWsMaxCtas) {
   switch (args.G) {
-    case 32: return launch<1, FUSED>(args, qw, qz, sc, ar, stream);
-    case 64: return launch<2, FUSED>(args, qw, qz, sc, ar, stream);
-    default: return launch<4, FUSED>(args, qw, qz, sc, ar, stream);
+    case 32: return launch<1, FUSED>(args, qw, qz, sc, ar, max_ctas, stream);
+    case 64: return launch<2, FUSED>(args, qw, qz, sc, ar, max_ctas, stream);
+    default: return launch<4, FUSED>(args, qw, qz, sc, ar, max_ctas, stream);
   }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Scratch for b2_w4_gemm_noalloc: a fixed array in device memory, created when the library is
+// loaded on a device and kept until the process exits. Layout: [status 256 B][arrival counters of
+// up to kNoAllocMaxTiles output tiles][two fp32 partial slots for each of up to kNoAllocMaxCtas
+// CTAs]. 2,113,792 bytes per device.
+// ------------------------------------------------------------------------------------------------
+constexpr int kNoAllocMaxTiles = 4096;  // N <= 4096 * 128 = 524288 output columns
+constexpr int kNoAllocMaxCtas = 256;
+constexpr size_t kNoAllocCountersOff = 256;
+constexpr size_t kNoAllocPartialsOff = kNoAllocCountersOff + (size_t)kNoAllocMaxTiles * 4;
+constexpr size_t kNoAllocBytes =
+    kNoAllocPartialsOff + (size_t)kNoAllocMaxCtas * 2 * kSlotFloats * sizeof(float);
+static_assert(kNoAllocPartialsOff % 256 == 0, "partial slots stay 256-byte aligned");
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+// Device address of g_noalloc_scratch, looked up once per device. In host code the name
+// g_noalloc_scratch is only a host-side stand-in for the symbol; a kernel must be given the
+// address cudaGetSymbolAddress returns for the current device.
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[64] = {nullptr};
+
+int noalloc_scratch(unsigned char** out) {
+  int dev = 0;
+  B2_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(B2_ERR_UNSUPPORTED, "w4_noalloc: device ordinal %d", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(B2_ERR_CUDA, "w4_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    // The counters must start at zero; the kernel leaves them at zero after every call.
+    e = cudaMemset(p, 0, kNoAllocPartialsOff);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess)
+      return fail(B2_ERR_CUDA, "w4_noalloc: clearing the scratch failed: %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return B2_OK;
 }
 
 }  // namespace
@@ -598,6 +655,28 @@ int launch_w4(const void* a, const void* qw, const void* qz, const void* sc, voi
   int rc = validate(a, qw, qz, sc, y, M, K, N, G, ws, ws_bytes);
   if (rc) return rc;
   return dispatch<false>(make_args(a, y, M, K, N, G, ws), qw, qz, sc, nullptr, stream);
+}
+
+int launch_w4_noalloc(const void* a, const void* qw, const void* qz, const void* sc, void* y, int M,
+                      int K, int N, int G, cudaStream_t stream) {
+  const int tiles = (N + kTileN - 1) / kTileN;
+  if (N > 0 && tiles > kNoAllocMaxTiles)
+    return fail(B2_ERR_INVALID_ARG,
+                "w4_noalloc: N=%d needs %d output tiles; the fixed scratch holds at most %d "
+                "(N <= %d)", N, tiles, kNoAllocMaxTiles, kNoAllocMaxTiles * kTileN);
+  unsigned char* scratch = nullptr;
+  int rc = validate(a, qw, qz, sc, y, M, K, N, G);
+  if (rc) return rc;
+  rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  W4Args args = make_args(a, y, M, K, N, G, scratch);
+  args.status = reinterpret_cast<int*>(scratch);
+  args.counters = reinterpret_cast<int*>(scratch + kNoAllocCountersOff);
+  args.partials = reinterpret_cast<float*>(scratch + kNoAllocPartialsOff);
+  // Clear the status word and the counters this call uses: the array keeps whatever the last
+  // call left, and a call that gave up on a wait may have left counters behind.
+  B2_CUDA_TRY(cudaMemsetAsync(scratch, 0, kNoAllocCountersOff + (size_t)tiles * 4, stream));
+  return dispatch<false>(args, qw, qz, sc, nullptr, stream, kNoAllocMaxCtas);
 }
 
 int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* qz, const void* sc,
@@ -629,4 +708,11 @@ extern "C" int b2_w4_gemm_allreduce(b2_nvar* ar, const void* a, const void* qw, 
   if (!ar) return b2::fail(B2_ERR_STATE, "w4_allreduce: null all-reduce handle");
   return b2::launch_w4_allreduce(ar, a, qw, qz, sc, y, M, K, N, group_size, ws, ws_bytes,
                                  static_cast<cudaStream_t>(stream));
+}
+
+// The W4A16 GEMM without a caller-supplied workspace; see include/b2_skinny.h.
+extern "C" int b2_w4_gemm_noalloc(const void* a, const void* qw, const void* qz, const void* sc,
+                                  void* y, int M, int K, int N, int group_size, void* stream) {
+  return b2::launch_w4_noalloc(a, qw, qz, sc, y, M, K, N, group_size,
+                               static_cast<cudaStream_t>(stream));
 }
