@@ -84,7 +84,6 @@ __global__ void __launch_bounds__(kThreads) nvar_kernel(const uint4* in, uint4* 
     for (int r = 0; r < v.world; ++r)
       reinterpret_cast<uint4*>(ar_slot(v, r, par, v.rank))[i] = val;
   }
-  __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
     ar_publish(v, blockIdx.x, e);

@@ -54,10 +54,13 @@ __device__ __forceinline__ uint32_t ar_begin(const ArView& v) {
   return *reinterpret_cast<volatile uint32_t*>(&ar_header(v)->gen) + 1u;
 }
 
-// Publish piece `idx` of generation e on every rank. Call after this CTA's data stores and a
-// __threadfence_system() by every storing thread, from one thread.
+// Publish piece `idx` of generation e on every rank, from one thread, after a CTA barrier that
+// follows the CTA's data stores. The barrier orders the other threads' stores before this
+// thread's system-scope release fence, which (being cumulative) makes all of them visible on every
+// GPU before any flag is.
 __device__ __forceinline__ void ar_publish(const ArView& v, int idx, uint32_t e) {
-  for (int r = 0; r < v.world; ++r) st_release_sys(ar_flag(v, r, v.rank, idx), e);
+  __threadfence_system();
+  for (int r = 0; r < v.world; ++r) st_relaxed_sys(ar_flag(v, r, v.rank, idx), e);
 }
 
 // Wait until every rank has published piece `idx` of generation e here. Bounded: after

@@ -458,9 +458,8 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
           if (2 * t + j < p.M) *reinterpret_cast<float4*>(dst + (size_t)(2 * t + j) * p.N + n) = v[j];
       }
     }
-    __threadfence_system();
     named_bar_sync(1, kWarps * 32);
-    if (threadIdx.x == 0) ar_publish(ar, tile, e);
+    if (threadIdx.x == 0) ar_publish(ar, tile, e);  // one release fence covers the CTA's stores
   }
   if (!ok && lane == 0) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
   if constexpr (FUSED) {

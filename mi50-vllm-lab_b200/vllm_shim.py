@@ -83,6 +83,8 @@ class NvlinkAllReduce:
     it uses ``nvar_*``. ``ops`` can be replaced (tests inject a host-only fake).
     """
 
+    _instances = 0
+
     def __init__(self, cpu_group, rank: int, ranks: list[int], lib: str | None = None,
                  slot_bytes: int | None = None, ops=None):
         import torch.distributed as dist
@@ -94,7 +96,9 @@ class NvlinkAllReduce:
         self.rank = rank
         self.world = len(ranks)
         self.max_bytes = int(slot_bytes or self.ops.hostar_max_bytes())
-        name = [f"/b2_nvar_{os.getpid()}_{ranks[0]}" if rank == 0 else None]
+        NvlinkAllReduce._instances += 1
+        name = [f"/b2_nvar_{os.getpid()}_{ranks[0]}_{NvlinkAllReduce._instances}"
+                if rank == 0 else None]
         dist.broadcast_object_list(name, src=ranks[0], group=cpu_group)
         two = self.world == 2
         if rank == 0:
