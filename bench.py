@@ -364,6 +364,9 @@ SWEEP = (
     + [(f"drafter_fc_M{M}", "f16", M, 25600, 5120, 0) for M in (1, 8)]
     + [("check_w4_G32", "w4", 8, 5120, 1024, 32)]
 )
+# Extra cases for --profile only: the lm_head kernel on a 335 MB slice (above L2, small enough
+# for a multi-pass ncu capture); traffic scales with N for this kernel.
+PROFILE_ONLY = [("cfg1_lm_head_N32768", "f16", 7, 5120, 32768, 0)]
 
 
 def run_sweep(args):
@@ -380,6 +383,11 @@ def run_sweep(args):
     lib = capi.lib()
     torch.cuda.set_device(0)
     ws = torch.zeros(lib.b2_workspace_bytes(0), dtype=torch.uint8, device="cuda")
+    if args.no_pdl:
+        capi.check(lib.b2_set_tuning(3, 1), "b2_set_tuning")  # B2_TUNE_NO_PDL
+    for kv in args.tune:
+        k, v = (int(t) for t in kv.split("="))
+        capi.check(lib.b2_set_tuning(k, v), "b2_set_tuning")
     peak, _ = hbm_peak()
     l2 = torch.cuda.get_device_properties(0).L2_cache_size
 
@@ -461,7 +469,7 @@ def run_profile(args):
     lib = capi.lib()
     torch.cuda.set_device(0)
     ws = torch.zeros(lib.b2_workspace_bytes(0), dtype=torch.uint8, device="cuda")
-    name, kind, M, K, N, G = next(w for w in SWEEP if args.only in w[0])
+    name, kind, M, K, N, G = next(w for w in PROFILE_ONLY + list(SWEEP) if args.only in w[0])
     g = torch.Generator(device="cuda").manual_seed(5)
     x = torch.randn(M, K, device="cuda", generator=g).half()
     y = torch.empty(M, N, dtype=torch.float16, device="cuda")
@@ -483,6 +491,130 @@ def run_profile(args):
     print(json.dumps({"profiled": name, "launches": args.warmup + args.steps}))
 
 
+# the decode-verify step of a 64-layer W4A16 model at M = 8 (speculative k = 7),
+# tensor parallel over the ranks: qkv and gate_up column-parallel, o_proj and down_proj
+# row-parallel with the NVLink all-reduce fused into their epilogues, then the fp16 lm_head
+# (column-parallel, 151936 / P rows per rank), all captured in one CUDA graph.
+CFG4 = dict(layers=64, M=8, hidden=5120, qkv=8192, o_in=6144, inter=17408, vocab=151936, G=128)
+
+
+def decode_step_bytes(P: int) -> int:
+    c = CFG4
+    per_layer = (w4_bytes(c["M"], c["hidden"], c["qkv"] // P, c["G"])
+                 + w4_bytes(c["M"], c["o_in"] // P, c["hidden"], c["G"])
+                 + w4_bytes(c["M"], c["hidden"], 2 * c["inter"] // P, c["G"])
+                 + w4_bytes(c["M"], c["inter"] // P, c["hidden"], c["G"]))
+    return c["layers"] * per_layer + f16_bytes(c["M"], c["hidden"], c["vocab"] // P)
+
+
+def run_decode_step(args):
+    """Config 4 on N GPUs (TP = N): one graph replay per step, timed as the max over ranks."""
+    import torch
+
+    import __graft_entry__ as entry
+
+    rank, world, local = dist_setup(args.gpus)
+    pkg = entry.load_package()
+    from mi50_vllm_lab_b200 import vllm_shim
+
+    ops = pkg.ops()
+    c = CFG4
+    M, H, G, P = c["M"], c["hidden"], c["G"], world
+    ar = None
+    if P > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
+        ar = vllm_shim.NvlinkAllReduce(cpu, rank, list(range(P)), slot_bytes=M * H * 4)
+    g = torch.Generator(device="cuda").manual_seed(4000 + rank)
+
+    def w4(K, N):
+        return (torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32,
+                              generator=g),
+                torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda",
+                              dtype=torch.int32, generator=g),
+                (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half())
+
+    layers = [dict(qkv=w4(H, c["qkv"] // P), o=w4(c["o_in"] // P, H),
+                   gu=w4(H, 2 * c["inter"] // P), down=w4(c["inter"] // P, H))
+              for _ in range(c["layers"])]
+    lm = (torch.randn(c["vocab"] // P, H, device="cuda", generator=g) * 0.02).half()
+    x0 = torch.randn(M, H, device="cuda", generator=g).half()
+    # attention output and activated MLP input of this rank's shard (synthetic, fixed)
+    a_o = (torch.randn(M, c["o_in"] // P, device="cuda", generator=g) * 0.05).half()
+    a_d = (torch.randn(M, c["inter"] // P, device="cuda", generator=g) * 0.05).half()
+
+    def row_parallel(a, w):
+        return ar.w4_gemm_all_reduce(a, *w) if ar else ops.w4gemm(a, *w, 0, 0)
+
+    def step():
+        h = x0
+        for L in layers:
+            ops.w4gemm(h, *L["qkv"], 0, 0)
+            h = row_parallel(a_o, L["o"])
+            ops.w4gemm(h, *L["gu"], 0, 0)
+            h = row_parallel(a_d, L["down"])
+        return ops.gemm(h, lm, 0)
+
+    eager = step()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            out = step()
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    same = bool(torch.equal(out, eager))
+    st = torch.cuda.current_stream()
+    align = torch.zeros(1, device="cuda")
+    times = []
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            if P > 1:
+                import torch.distributed as dist
+
+                dist.all_reduce(align)  # line the ranks up on the device, not on the host
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            graph.replay()
+            e1.record(st)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1) * 1e3)
+    us = max_over_ranks(statistics.median(times), world)
+    status = ar.status() if ar else ops.workspace_status(False)
+    nbytes = decode_step_bytes(P)
+    peak, peak_kind = hbm_peak()
+    if rank == 0:
+        kernels = c["layers"] * 4 + 1
+        print(json.dumps({
+            "metric": "config 4: decode-verify step (64 W4A16 layers + fp16 lm_head, M=8), us per step",
+            "value": round(us, 1), "unit": "us", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": False, "scaling": "strong",
+            "dtype": "W4A16 / f16 (fp32 accumulate)", "data": "synthetic (seeded random weights)",
+            "config": {"workload": "config 4", "tp": P, "layers": c["layers"], "M": M,
+                       "kernels_per_step": kernels, "fused_allreduces_per_step": 2 * c["layers"] if P > 1 else 0,
+                       "graph": "one CUDA graph per step (programmatic dependent launch between GEMMs)",
+                       "per_rank_bytes_per_step": nbytes},
+            "per_rank_TBps": round(nbytes / us / 1e6, 3),
+            "roofline": {"bound": "hbm", "achieved": round(nbytes / us / 1e3, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(nbytes / us / 1e3 / peak, 4),
+                         "peak_source": peak_kind},
+            "graph_equals_eager": same, "device_status": status, "clocks": clk.summary()}),
+            flush=True)
+    del graph
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -490,10 +622,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--sweep", action="store_true")
+    ap.add_argument("--decode-step", action="store_true",
+                    help="config 4: the 64-layer decode-verify step in one CUDA graph, TP = --gpus")
     ap.add_argument("--only", default="", help="with --sweep/--profile: workloads whose name contains this")
     ap.add_argument("--profile", action="store_true", help="eager launches of one --only workload (for ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--tune", action="append", default=[], metavar="KEY=VALUE",
+                    help="with --sweep: b2_set_tuning(KEY, VALUE) first (B2_TUNE_* in b2_skinny.h)")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="with --sweep: launch each GEMM only after the previous one has finished")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -503,6 +641,8 @@ def main():
         run_profile(args)
     elif args.sweep:
         run_sweep(args)
+    elif args.decode_step:
+        run_decode_step(args)
     else:
         run_gpu(args)
 

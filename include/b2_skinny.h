@@ -67,6 +67,13 @@ int b2_abi_version(void);
  * leaves the counters at zero again. Calls that share a workspace must not overlap on the
  * GPU (issue them on one stream). Replaces the per-call at::empty split-K buffer of
  * kernels/w4.cu:330-334 and the separate w4_reduce_kernel launch (kernels/w4.cu:154-166).
+ *
+ * Early launch: b2_gemm_f16 and b2_w4_gemm use programmatic dependent launch. Their CTAs may
+ * start while the previous GEMM of this library on the stream is still finishing, and stream
+ * the first weight tiles (w; qw, qz, sc) into shared memory at once; activations, outputs,
+ * workspace and status are touched only after every earlier kernel on the stream has completed.
+ * Weights must therefore not be the output of another GEMM of this library on the same stream
+ * that may still be running; b2_set_tuning(B2_TUNE_NO_PDL, 1) turns early launch off.
  * ---------------------------------------------------------------------------------------- */
 
 /* Bytes of workspace that cover every supported shape on `device` (fixed per device). */
@@ -193,6 +200,8 @@ int b2_nvar_destroy(b2_nvar* ar);
  * ---------------------------------------------------------------------------------------- */
 #define B2_TUNE_CTAS_PER_SM 1     /* resident CTAs per SM the stream-K grid targets (0 = auto) */
 #define B2_TUNE_MIN_UNITS 2       /* fewest k-units per CTA before the grid shrinks (0 = auto)  */
+#define B2_TUNE_NO_PDL 3          /* nonzero: launch every kernel only after the previous one has
+                                     finished (no programmatic dependent launch)                 */
 int b2_set_tuning(int key, int value);
 int b2_get_tuning(int key);
 

@@ -77,11 +77,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
+// The same wait for the producer thread, which backs off between polls so that its warp does not
+// take issue slots from the consumer warps on the same scheduler while the ring is full.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort) {
+  if (mbar_test(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (unsigned int it = 1; it < kMaxSpin; ++it) {
+    __nanosleep(32);
+    if (mbar_test(bar, parity)) return true;
+    if ((it & 15u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kPipeWaitNs) break;
+    }
+  }
+  *abort = 1;
+  return false;
+}
+
 // ---------------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor, no multicast) and L2 policy
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
+}
+__device__ __forceinline__ uint64_t l2_evict_normal_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t p;
@@ -102,18 +125,23 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
 // ---------------------------------------------------------------------------------------------
 // Loads, stores, barriers
 // ---------------------------------------------------------------------------------------------
+// Not volatile, so the compiler may schedule them among independent arithmetic; the "memory"
+// clobber keeps them after the mbarrier waits (volatile asm with a "memory" clobber), which is
+// what orders them after the TMA writes they read.
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr));
+  asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "r"(addr)
+      : "memory");
   return v;
 }
 __device__ __forceinline__ uint4 ldg_nc128(const void* p) {
   uint4 v;
-  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
+  asm("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p)
+      : "memory");
   return v;
 }
 // Named barrier over the first `threads` threads of the CTA (the consumer warps).
@@ -134,13 +162,20 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// Programmatic dependent launch. grid_dep_wait() returns once the grids this one depends on
+// have completed and their memory is visible (at once when the launch has no such dependency);
+// grid_dep_launch() lets the next grid on the stream start launching its CTAs early.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // Tensor cores: D = A(16x16 f16, row) * B(16x8 f16, col) + C, fp32 accumulate.
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));

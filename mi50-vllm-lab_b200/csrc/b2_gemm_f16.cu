@@ -76,8 +76,12 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
     mbar_fence_init();
   }
   __syncthreads();
+  grid_dep_launch();
 
   // ------------------------------------------------------------------ producer warp (1 thread)
+  // The weights never come from the previous grid on the stream, so the producer streams them
+  // without waiting for it (programmatic dependent launch); the consumers wait before they
+  // read x or touch the workspace and y.
   if (warp == kWarps) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_w);
@@ -89,7 +93,7 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
 #pragma unroll
       for (int s = 0; s < kStages; ++s) used[s] = false, last_ph[s] = 0;
       for (UnitCursor cu(sk, u_lo, u_hi); cu.left > 0; cu.next(sk)) {
-        if (!mbar_wait(&empty[st], ph ^ 1u, s_abort)) break;
+        if (!mbar_wait_backoff(&empty[st], ph ^ 1u, s_abort)) break;
         mbar_arrive_expect_tx(&full[st], kStageBytes);
         tma_load_2d(smem + st * kStageBytes, &tm_w, &full[st], cu.ku * kUnitK, cu.tile * kTileN,
                     pol);
@@ -104,12 +108,16 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
         while (!mbar_test(&full[s], last_ph[s]) && globaltimer_ns() - t0 < kPipeWaitNs) {
         }
       }
-      if (*s_abort) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
+      if (*s_abort) {
+        grid_dep_wait();
+        atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
+      }
     }
     return;
   }
 
   // ------------------------------------------------------------------ consumer warps
+  grid_dep_wait();
   const int g = lane >> 2, t = lane & 3;
   const bool has_row = g < p.M;
   const __half* xrow = p.x + (size_t)(has_row ? g : 0) * p.K;
@@ -282,9 +290,8 @@ int launch_gemm_f16(const void* x, const void* w, void* y, int M, int K, int N, 
   a.status = reinterpret_cast<int*>(wsb);
   a.counters = reinterpret_cast<int*>(wsb + ws_counters_offset());
   a.partials = reinterpret_cast<float*>(wsb + ws_partials_offset());
-  gemm_f16_kernel<<<sk.ctas, kThreads, kSmemBytes, stream>>>(tm, a);
-  B2_CUDA_TRY(cudaGetLastError());
-  return B2_OK;
+  return launch_kernel(gemm_f16_kernel, sk.ctas, kThreads, kSmemBytes, stream, /*early=*/true, tm,
+                       a);
 }
 
 }  // namespace b2

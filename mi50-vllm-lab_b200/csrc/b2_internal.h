@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "b2_skinny.h"
 
 namespace b2 {
@@ -49,5 +51,26 @@ int tuning(int key);
 int streamk_ctas(long long total, int sm_count, int occ, int min_units_default);
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launch `kernel` on `stream`. With `early` the launch is marked for programmatic dependent
+// launch: its CTAs may start while the previous kernel on the stream is finishing, and they read
+// nothing that kernel writes before grid_dep_wait(). B2_TUNE_NO_PDL != 0 turns this off.
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kernel)(KArgs...), int grid, int block, size_t smem, cudaStream_t stream,
+                  bool early, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (early && tuning(B2_TUNE_NO_PDL) == 0) ? 1 : 0;
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
 
 }  // namespace b2

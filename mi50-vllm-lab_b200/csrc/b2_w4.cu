@@ -3,20 +3,23 @@
 // Replaces w4_gemm / w4_skinny_s_kernel / w4_reduce_kernel of kernels/w4.cu:154-346,479-504 with
 // the same operand layouts (kernels/w4.cu:477-478): a [M,K] fp16, qw [K/8,N] int32, qz [K/G,N/8]
 // int32 (v2 zeros), sc [K/G,N] fp16. Design:
-//   - a producer warp streams 128-column x 128-k units (8 KB of qw plus that unit's scale and
-//     zero rows) into a ring of shared-memory stages with TMA (128-byte swizzle for qw,
-//     L2 evict-first);
+//   - one thread of a producer warp streams 128-column x 128-k units (8 KB of qw, that unit's
+//     scale and zero rows, and the unit's activations, 8 rows x 128 k = 2 KB) into a ring of
+//     shared-memory stages with TMA (128-byte swizzle for qw and x, L2 evict-first for the
+//     weights), so every activation is read from L2 once per CTA unit instead of once per warp;
 //   - each of four consumer warps owns 32 columns of the unit. A lane reads one 16-byte chunk
-//     (4 columns of one 8-k word row) per 32 k, unpacks the 8 nibbles of each word to
-//     (q - z) in fp16 exactly (magic-number 1024 trick with zero constants built from integer
-//     bits) and feeds them to mma.sync m16n8k16 as the A operand against the <= 8 activation
-//     rows (B operand). Each weight is dequantized once and used for all M rows.
+//     (4 columns of one 8-k word row) per 32 k, unpacks the 8 nibbles of each word to (q - z)
+//     in fp16 exactly (lop3 magic-number trick + add.f16x2) and feeds them to mma.sync
+//     m16n8k16 as the A operand against the <= 8 activation rows (B operand). Each weight is
+//     dequantized once and used for all M rows.
 //   - (q - z) * x is accumulated per quantization group in fp32 and multiplied by the group's
 //     scale in fp32 once per group, so no product is rounded to fp16 (the reference rounds
 //     (q - z) * s to fp16 per weight, kernels/w4.cu:33-36).
 //   - stream-K over a persistent grid; tiles shared by CTAs are summed by the last CTA to
 //     finish, in CTA order, from fp32 slots (one launch; replaces the workspace + second
 //     reduce kernel of kernels/w4.cu:154-166,330-346).
+//   - programmatic dependent launch: the first weight stages are requested before the kernel
+//     waits for the previous grid on the stream; activations, workspace and y come after.
 //   - optionally the NVLink all-reduce of a row-parallel layer is fused into the epilogue: the
 //     finished fp32 tile is pushed to every rank, and each rank adds the ranks' tiles in rank
 //     order (bit-identical on every rank).
@@ -47,20 +50,25 @@ constexpr int align128(int v) { return (v + 127) & ~127; }
 // start on a 128-byte boundary, and the swizzled qw boxes on a 1024-byte one.
 template <int GP>  // GP: 32-k pairs per scale group inside a unit (1: G=32, 2: G=64, 4: G>=128)
 struct Cfg {
-  // Stages per CTA: 6 x 8.5 KB lets four CTAs (16 consumer warps) share an SM's 228 KB when
-  // G >= 128 (the exact-dequant variants need more registers and run three CTAs per SM).
-  static constexpr int kStages = 6;
+  // 5 stages x 10.6 KB let four CTAs (16 consumer warps) share an SM's 228 KB when G >= 128
+  // (the exact-dequant variants need more registers and run three CTAs per SM).
+  static constexpr int kStages = 5;
   static constexpr int RG = 4 / GP;                        // group rows per unit
   static constexpr int kScBytes = RG * kTileN * 2;         // scales of one unit
   static constexpr int kQzBytes = RG * (kTileN / 8) * 4;   // zeros of one unit
   static constexpr int kScStride = align128(kScBytes);
   static constexpr int kQzStride = align128(kQzBytes);
-  static constexpr int kTx = kQwStage + kScBytes + kQzBytes;
-  static constexpr int kScOff = kStages * kQwStage;
+  // activations of one unit, x[8 rows][128 k] fp16: two TMA boxes of 64 k x 8 rows, 128-byte
+  // swizzle (chunk c of row m of box b at b * 1024 + m * 128 + ((c ^ m) << 4))
+  static constexpr int kXBytes = kMaxM * kUnitK * 2;
+  static constexpr int kTx = kQwStage + kXBytes + kScBytes + kQzBytes;
+  static constexpr int kXOff = kStages * kQwStage;
+  static constexpr int kScOff = kXOff + kStages * kXBytes;
   static constexpr int kQzOff = kScOff + kStages * kScStride;
   static constexpr int kBarOff = kQzOff + kStages * kQzStride;
   static constexpr int kSmem = 1024 + kBarOff + 2 * kStages * 8 + 32;
   static_assert(kQwBox % 1024 == 0 && kQwStage % 1024 == 0, "swizzled boxes need 1024 B");
+  static_assert(kXOff % 1024 == 0 && kXBytes % 1024 == 0, "swizzled boxes need 1024 B");
   static_assert(kScOff % 128 == 0 && kScStride % 128 == 0, "TMA destination alignment");
   static_assert(kQzOff % 128 == 0 && kQzStride % 128 == 0, "TMA destination alignment");
   static_assert(kBarOff % 8 == 0, "mbarrier alignment");
@@ -86,30 +94,22 @@ __device__ __forceinline__ uint32_t hadd2_u(uint32_t a, uint32_t b) {
   asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
-__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
 
 // (q - z) for the 8 nibbles of one shuffled word, as four fp16 pairs in k order
 // (k0,k1) (k2,k3) (k4,k5) (k6,k7). Nibble i sits at bits 4i (k = 2i) and nibble 4+i at bits
-// 16+4i (k = 2i+1). OR-ing a nibble into the mantissa of fp16 1024.0 (0x6400) gives 1024 + q for
-// the low nibble of a byte and 1024 + 16q for the high one. zlo = -(1024 + z) and
-// zhi = -(64 + z) in both halves; all steps are exact in fp16.
+// 16+4i (k = 2i+1). OR-ing a low nibble (bits 0..3 of a half) into the mantissa of fp16 1024.0
+// (0x6400, ulp 1) gives 1024 + q; OR-ing a high nibble (bits 4..7) into fp16 64.0 (0x5400,
+// ulp 1/16) gives 64 + q. zlo = -(1024 + z) and zhi = -(64 + z) in both halves; every step is
+// exact in fp16: four lop3, one shift, four add.f16x2.
 __device__ __forceinline__ void dequant_word(uint32_t q, uint32_t zlo, uint32_t zhi,
                                              uint32_t (&d)[4]) {
-  constexpr uint32_t kMagic = 0x64006400u;      // 1024.0 | 1024.0
-  constexpr uint32_t kSixteenth = 0x2C002C00u;  // 0.0625 | 0.0625
-  const uint32_t lo0 = lop_and_or(q, 0x000F000Fu, kMagic);
-  const uint32_t hi0 = lop_and_or(q, 0x00F000F0u, kMagic);
+  constexpr uint32_t kLo = 0x64006400u;  // 1024.0 | 1024.0
+  constexpr uint32_t kHi = 0x54005400u;  // 64.0 | 64.0
   const uint32_t q8 = q >> 8;
-  const uint32_t lo1 = lop_and_or(q8, 0x000F000Fu, kMagic);
-  const uint32_t hi1 = lop_and_or(q8, 0x00F000F0u, kMagic);
-  d[0] = hadd2_u(lo0, zlo);
-  d[1] = hfma2_u(hi0, kSixteenth, zhi);
-  d[2] = hadd2_u(lo1, zlo);
-  d[3] = hfma2_u(hi1, kSixteenth, zhi);
+  d[0] = hadd2_u(lop_and_or(q, 0x000F000Fu, kLo), zlo);
+  d[1] = hadd2_u(lop_and_or(q, 0x00F000F0u, kHi), zhi);
+  d[2] = hadd2_u(lop_and_or(q8, 0x000F000Fu, kLo), zlo);
+  d[3] = hadd2_u(lop_and_or(q8, 0x00F000F0u, kHi), zhi);
 }
 
 // Lane output layout of a 128-column tile: lane (g, t) of warp w owns columns
@@ -131,56 +131,26 @@ __device__ __forceinline__ void store_y(const W4Args& p, int tile, int colw, int
   }
 }
 
-__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-
-// The eight nibbles of one word as 1024 + q (low nibble of a byte, k = 0,1 and 4,5 of the word)
-// or 1024 + 16q (high nibble, k = 2,3 and 6,7), exact fp16, without subtracting anything: four
-// lop3 and one shift. The offsets are removed after the dot product (see the kernel comment).
-__device__ __forceinline__ void magic_word(uint32_t q, uint32_t (&d)[4]) {
-  constexpr uint32_t kMagic = 0x64006400u;
-  const uint32_t q8 = q >> 8;
-  d[0] = lop_and_or(q, 0x000F000Fu, kMagic);
-  d[1] = lop_and_or(q, 0x00F000F0u, kMagic);
-  d[2] = lop_and_or(q8, 0x000F000Fu, kMagic);
-  d[3] = lop_and_or(q8, 0x00F000F0u, kMagic);
-}
-
-// float(z) for 0 <= z < 2^23 without the conversion unit
-__device__ __forceinline__ float small_uint_to_float(uint32_t z) {
-  return __int_as_float(0x4B000000 | z) - 8388608.0f;
-}
-
-// Two ways to turn a word into the mma A operand, chosen by the group size:
-//  * EXACT (G = 32, 64): A = (q - z) in fp16 (lop3 + add/fma.f16x2, exact); the fp32 sum of a
-//    group is scaled once: acc += s * sum.
-//  * OFFSET (G >= 128): A = 1024 + q or 1024 + 16q (lop3 only) and B = x or x/16 (the activation
-//    pairs of high nibbles pre-scaled by 1/16, exact), so the dot product of a group is
-//        P = sum_k q_k x_k + C,   C = 1024 * sum_{low k} x + 64 * sum_{high k} x.
-//    Two more mma per 32 k with constant A rows (1024 | 1024 gives C; 1 | 16 gives S = sum x)
-//    produce C and S in fp32, and the fold is acc += s * (P - C - z * S). This removes the four
-//    fp16 subtractions per word from the inner loop; the price is that P and C carry an offset of
-//    ~1024 * |sum x| that cancels in fp32 (about 1e-4 of |y| at these sizes, below the fp16
-//    rounding of the output).
+// A = (q - z) in fp16 (exact, see dequant_word) against B = x; the fp32 sum of each quantization
+// group is scaled once: acc += s * sum. Every weight is dequantized once per CTA and used for all
+// M rows.
 template <int GP, bool FUSED>
 __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
     w4_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_sc,
-              const __grid_constant__ CUtensorMap tm_qz, const W4Args p, const ArView ar) {
+              const __grid_constant__ CUtensorMap tm_qz, const __grid_constant__ CUtensorMap tm_x,
+              const W4Args p, const ArView ar) {
   using C = Cfg<GP>;
   constexpr int RG = C::RG;
   constexpr int kStages = C::kStages;
-  constexpr bool OFFSET = (GP == 4);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* s_qw = smem;
+  uint8_t* s_x = smem + C::kXOff;    // stage st at s_x + st * kXBytes
   uint8_t* s_sc = smem + C::kScOff;  // stage st at s_sc + st * kScStride: [RG][128] fp16
   uint8_t* s_qz = smem + C::kQzOff;  // stage st at s_qz + st * kQzStride: [RG][16] int32
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
-  uint64_t* empty = full + kStages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);  // TMA bytes landed
+  uint64_t* empty = full + kStages;                                 // consumers done
   volatile int* s_abort = reinterpret_cast<volatile int*>(empty + kStages);
   volatile int* s_flag = s_abort + 1;
   volatile uint32_t* s_gen = reinterpret_cast<volatile uint32_t*>(s_abort + 2);
@@ -196,10 +166,10 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
     }
     *s_abort = 0;
     *s_flag = 0;
-    if (FUSED) *s_gen = ar_begin(ar);
     mbar_fence_init();
   }
   __syncthreads();
+  grid_dep_launch();
 
   // ------------------------------------------------------------------ producer warp (1 thread)
   if (warp == kWarps) {
@@ -207,33 +177,51 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
       tma_prefetch_desc(&tm_qw);
       tma_prefetch_desc(&tm_sc);
       tma_prefetch_desc(&tm_qz);
-      const uint64_t pol = l2_evict_first_policy();
-      int st = 0;
-      uint32_t ph = 0;
-      uint32_t last_ph[kStages];
-      bool used[kStages];
-#pragma unroll
-      for (int s = 0; s < kStages; ++s) used[s] = false, last_ph[s] = 0;
-      for (UnitCursor cu(sk, u_lo, u_hi); cu.left > 0; cu.next(sk)) {
-        if (!mbar_wait(&empty[st], ph ^ 1u, s_abort)) break;
-        const int ku = cu.ku;
-        const int n0 = cu.tile * kTileN;
-        const int grow = (ku * kUnitK) / p.G;
+      tma_prefetch_desc(&tm_x);
+      const uint64_t pol_w = l2_evict_first_policy();   // weights: read once
+      const uint64_t pol_x = l2_evict_normal_policy();  // activations: read by every CTA
+      auto issue_w = [&](int st, const UnitCursor& c) {
+        const int n0 = c.tile * kTileN;
+        const int grow = (c.ku * kUnitK) / p.G;
         mbar_arrive_expect_tx(&full[st], C::kTx);
 #pragma unroll
         for (int w = 0; w < kWarps; ++w)
-          tma_load_2d(s_qw + st * kQwStage + w * kQwBox, &tm_qw, &full[st], n0 + 32 * w, ku * 16,
-                      pol);
-        tma_load_2d(s_sc + st * C::kScStride, &tm_sc, &full[st], n0, grow, pol);
-        tma_load_2d(s_qz + st * C::kQzStride, &tm_qz, &full[st], n0 / 8, grow, pol);
-        used[st] = true;
-        last_ph[st] = ph;
+          tma_load_2d(s_qw + st * kQwStage + w * kQwBox, &tm_qw, &full[st], n0 + 32 * w,
+                      c.ku * 16, pol_w);
+        tma_load_2d(s_sc + st * C::kScStride, &tm_sc, &full[st], n0, grow, pol_w);
+        tma_load_2d(s_qz + st * C::kQzStride, &tm_qz, &full[st], n0 / 8, grow, pol_w);
+      };
+      auto issue_x = [&](int st, const UnitCursor& c) {
+        tma_load_2d(s_x + st * C::kXBytes, &tm_x, &full[st], c.ku * kUnitK, 0, pol_x);
+        tma_load_2d(s_x + st * C::kXBytes + 1024, &tm_x, &full[st], c.ku * kUnitK + 64, 0, pol_x);
+      };
+      // Weights never come from the previous grid on the stream: request the first stages
+      // before waiting for it; their activations follow once it has completed.
+      const UnitCursor c0(sk, u_lo, u_hi);
+      UnitCursor c = c0;
+      int issued = 0;
+      for (; issued < kStages && c.left > 0; ++issued, c.next(sk)) issue_w(issued, c);
+      grid_dep_wait();
+      {
+        UnitCursor cx = c0;
+        for (int j = 0; j < issued; ++j, cx.next(sk)) issue_x(j, cx);
+      }
+      int st = 0;
+      uint32_t ph = 0;  // parity of the consumers' release of the unit kStages back
+      for (; c.left > 0; ++issued, c.next(sk)) {
+        if (!mbar_wait_backoff(&empty[st], ph, s_abort)) break;
+        issue_w(st, c);
+        issue_x(st, c);
         if (++st == kStages) st = 0, ph ^= 1u;
       }
-      for (int s = 0; s < kStages; ++s) {
-        if (!used[s]) continue;
+      // Do not retire while copies this thread issued may still be landing in shared memory:
+      // units 0..issued-1 were requested; the last unit of stage s is the largest u < issued
+      // with u % kStages == s.
+      for (int s = 0; s < kStages && s < issued; ++s) {
+        const int u = s + ((issued - 1 - s) / kStages) * kStages;
+        const uint32_t par = (uint32_t)((u / kStages) & 1);
         const unsigned long long t0 = globaltimer_ns();
-        while (!mbar_test(&full[s], last_ph[s]) && globaltimer_ns() - t0 < kPipeWaitNs) {
+        while (!mbar_test(&full[s], par) && globaltimer_ns() - t0 < kPipeWaitNs) {
         }
       }
       if (*s_abort) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
@@ -242,57 +230,36 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
   }
 
   // ------------------------------------------------------------------ consumer warps
+  grid_dep_wait();
+  if (FUSED && threadIdx.x == 0) *s_gen = ar_begin(ar);
+  named_bar_sync(1, kWarps * 32);
   const int g = lane >> 2, t = lane & 3;
   const int ch = ((g & 1) << 2) | (g >> 1);  // 16-byte chunk (4 columns) of the 128-byte row
   const int colw = warp * 32 + ch * 4;       // lane's first column inside the tile
-  const bool has_row = g < p.M;
-  const __half* xrow = p.x + (size_t)(has_row ? g : 0) * p.K;
   const uint32_t e = FUSED ? *s_gen : 0u;
-  // constant A rows of the correction mma (OFFSET): row 0 = 1024 everywhere (C), row 1 = 1 on
-  // low-nibble k and 16 on high-nibble k (S); rows 2..15 zero
-  const uint32_t cs_lo = g == 0 ? 0x64006400u : (g == 1 ? 0x3C003C00u : 0u);
-  const uint32_t cs_hi = g == 0 ? 0x64006400u : (g == 1 ? 0x4C004C00u : 0u);
 
-  float acc[2][4], accg[2][4], acs[4];
+  float acc[2][4], accg[2][4];
 #pragma unroll
   for (int T = 0; T < 2; ++T)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[T][i] = accg[T][i] = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) acs[i] = 0.f;
-
-  auto load_x = [&](int ku_, uint4 (&dst)[4]) {
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      dst[q] = has_row ? ldg_nc128(xrow + ku_ * kUnitK + 32 * q + 8 * t) : make_uint4(0, 0, 0, 0);
-  };
-  uint4 xn[4];
-  {
-    UnitCursor c0(sk, u_lo, u_hi);
-    load_x(c0.ku, xn);
-  }
 
   int st = 0;
   uint32_t ph = 0;
   bool ok = true;
   for (UnitCursor cu(sk, u_lo, u_hi); cu.left > 0; cu.next(sk)) {
-    const int tile = cu.tile, ku = cu.ku;
+    const int tile = cu.tile;
+    if (ok) ok = mbar_wait(&full[st], ph, s_abort);
+
+    // activations: lane (g, t) takes chunk 4q + t of row g (box q / 2), the k of its A chunk
+    const uint32_t xb = smem_u32(s_x + st * C::kXBytes) + g * 128;
     uint4 xv[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) xv[q] = xn[q];
-    if (cu.left > 1) load_x(ku + 1 == sk.upt ? 0 : ku + 1, xn);  // next unit's activations
-    if (OFFSET) {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {  // high-nibble pairs (k 2,3 and 6,7 of each 8) times 1/16
-        xv[q].y = hmul2_u(xv[q].y, 0x2C002C00u);
-        xv[q].w = hmul2_u(xv[q].w, 0x2C002C00u);
-      }
-    }
-    if (ok) ok = mbar_wait(&full[st], ph, s_abort);
+    for (int q = 0; q < 4; ++q) xv[q] = lds128(xb + (q >> 1) * 1024 + ((((4 * q + t) & 7) ^ g) << 4));
 
     // zero points and scales of the lane's 4 columns for each group row of the unit
     uint32_t zlo[RG][4], zhi[RG][4];
-    float scl[RG][4], zf[RG][4];
+    float scl[RG][4];
 #pragma unroll
     for (int r = 0; r < RG; ++r) {
       const uint32_t* qz_row =
@@ -309,12 +276,8 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint32_t z = (zw >> (4 * i)) & 0xFu;
-        if (OFFSET) {
-          zf[r][i] = small_uint_to_float(z);
-        } else {
-          zlo[r][i] = (0xE400u + z) * 0x00010001u;         // -(1024 + z)
-          zhi[r][i] = (0xD400u + (z << 4)) * 0x00010001u;  // -(64 + z)
-        }
+        zlo[r][i] = (0xE400u + z) * 0x00010001u;         // -(1024 + z)
+        zhi[r][i] = (0xD400u + (z << 4)) * 0x00010001u;  // -(64 + z)
       }
     }
 
@@ -325,27 +288,16 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
       const uint4 w = lds128(qb + row * 128 + ((ch ^ (row & 7)) << 4));
       const int r = (RG == 1) ? 0 : (q / GP);
       uint32_t d0[4], d1[4], d2[4], d3[4];
-      if (OFFSET) {
-        magic_word(w.x, d0);
-        magic_word(w.y, d1);
-        magic_word(w.z, d2);
-        magic_word(w.w, d3);
-      } else {
-        dequant_word(w.x, zlo[r][0], zhi[r][0], d0);
-        dequant_word(w.y, zlo[r][1], zhi[r][1], d1);
-        dequant_word(w.z, zlo[r][2], zhi[r][2], d2);
-        dequant_word(w.w, zlo[r][3], zhi[r][3], d3);
-      }
+      dequant_word(w.x, zlo[r][0], zhi[r][0], d0);
+      dequant_word(w.y, zlo[r][1], zhi[r][1], d1);
+      dequant_word(w.z, zlo[r][2], zhi[r][2], d2);
+      dequant_word(w.w, zlo[r][3], zhi[r][3], d3);
       // n-tile 0: A rows g / g+8 = columns colw / colw+1; n-tile 1: colw+2 / colw+3
       mma_16816(accg[0], d0[0], d1[0], d0[1], d1[1], xv[q].x, xv[q].y);
       mma_16816(accg[0], d0[2], d1[2], d0[3], d1[3], xv[q].z, xv[q].w);
       mma_16816(accg[1], d2[0], d3[0], d2[1], d3[1], xv[q].x, xv[q].y);
       mma_16816(accg[1], d2[2], d3[2], d2[3], d3[3], xv[q].z, xv[q].w);
-      if (OFFSET) {
-        mma_16816(acs, cs_lo, 0u, cs_hi, 0u, xv[q].x, xv[q].y);
-        mma_16816(acs, cs_lo, 0u, cs_hi, 0u, xv[q].z, xv[q].w);
-      }
-      if (!OFFSET && (q + 1) % GP == 0) {
+      if ((q + 1) % GP == 0) {
 #pragma unroll
         for (int T = 0; T < 2; ++T)
 #pragma unroll
@@ -354,25 +306,6 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
             accg[T][i] = 0.f;
           }
       }
-    }
-    if (OFFSET) {
-      // C[m], S[m] for this lane's rows m = 2t, 2t+1 live in lanes t (row 0) and 4+t (row 1)
-      const float c0 = __shfl_sync(0xffffffffu, acs[0], t);
-      const float c1 = __shfl_sync(0xffffffffu, acs[1], t);
-      const float s0 = __shfl_sync(0xffffffffu, acs[0], 4 + t);
-      const float s1 = __shfl_sync(0xffffffffu, acs[1], 4 + t);
-#pragma unroll
-      for (int T = 0; T < 2; ++T)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int col = 2 * T + (i >> 1);
-          const float cm = (i & 1) ? c1 : c0, sm = (i & 1) ? s1 : s0;
-          const float d = fmaf(-zf[0][col], sm, accg[T][i] - cm);
-          acc[T][i] = fmaf(scl[0][col], d, acc[T][i]);
-          accg[T][i] = 0.f;
-        }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acs[i] = 0.f;
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
@@ -502,7 +435,7 @@ KernelCache g_cache[64][3][2];
 
 template <int GP, bool FUSED>
 int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, const ArView* ar,
-           int max_ctas, cudaStream_t stream) {
+           int max_ctas, bool early, cudaStream_t stream) {
   using C = Cfg<GP>;
   W4Args a = a0;
   DeviceInfo di;
@@ -531,7 +464,7 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
   }
   a.sk = sk;
 
-  CUtensorMap m_qw, m_sc, m_qz;
+  CUtensorMap m_qw, m_sc, m_qz, m_x;
   rc = encode_2d(&m_qw, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, (uint64_t)N, (uint64_t)(K / 8),
                  (uint64_t)N * 4, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
@@ -541,10 +474,13 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
   rc = encode_2d(&m_qz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, (uint64_t)(N / 8), (uint64_t)(K / G),
                  (uint64_t)N / 2, kTileN / 8, C::RG, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (rc) return rc;
-  ArView none{};
-  kern<<<sk.ctas, kThreads, C::kSmem, stream>>>(m_qw, m_sc, m_qz, a, ar ? *ar : none);
-  B2_CUDA_TRY(cudaGetLastError());
-  return B2_OK;
+  // activations [M rows, K] fp16; rows M..7 of a box read as zeros (out of bounds)
+  rc = encode_2d(&m_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)K, (uint64_t)a.M,
+                 (uint64_t)K * 2, 64, kMaxM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  const ArView view = ar ? *ar : ArView{};
+  return launch_kernel(kern, sk.ctas, kThreads, C::kSmem, stream, early && !FUSED, m_qw, m_sc,
+                       m_qz, m_x, a, view);
 }
 
 int validate(const void* a, const void* qw, const void* qz, const void* sc, const void* y, int M,
@@ -594,13 +530,15 @@ W4Args make_args(const void* a, void* y, int M, int K, int N, int G, void* ws) {
   return r;
 }
 
+// `early`: programmatic dependent launch (the plain GEMM only; the fused all-reduce and the
+// no-alloc variant, which clears its scratch with a memset just before, launch normally).
 template <bool FUSED>
 int dispatch(const W4Args& args, const void* qw, const void* qz, const void* sc, const ArView* ar,
-             cudaStream_t stream, int max_ctas = kWsMaxCtas) {
+             cudaStream_t stream, int max_ctas = kWsMaxCtas, bool early = false) {
   switch (args.G) {
-    case 32: return launch<1, FUSED>(args, qw, qz, sc, ar, max_ctas, stream);
-    case 64: return launch<2, FUSED>(args, qw, qz, sc, ar, max_ctas, stream);
-    default: return launch<4, FUSED>(args, qw, qz, sc, ar, max_ctas, stream);
+    case 32: return launch<1, FUSED>(args, qw, qz, sc, ar, max_ctas, early, stream);
+    case 64: return launch<2, FUSED>(args, qw, qz, sc, ar, max_ctas, early, stream);
+    default: return launch<4, FUSED>(args, qw, qz, sc, ar, max_ctas, early, stream);
   }
 }
 
@@ -653,7 +591,8 @@ int launch_w4(const void* a, const void* qw, const void* qz, const void* sc, voi
               int N, int G, void* ws, size_t ws_bytes, cudaStream_t stream) {
   int rc = validate(a, qw, qz, sc, y, M, K, N, G, ws, ws_bytes);
   if (rc) return rc;
-  return dispatch<false>(make_args(a, y, M, K, N, G, ws), qw, qz, sc, nullptr, stream);
+  return dispatch<false>(make_args(a, y, M, K, N, G, ws), qw, qz, sc, nullptr, stream,
+                         kWsMaxCtas, /*early=*/true);
 }
 
 int launch_w4_noalloc(const void* a, const void* qw, const void* qz, const void* sc, void* y, int M,
