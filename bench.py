@@ -451,7 +451,7 @@ def run_sweep(args):
                 "bytes": nb, "l2_rotation_copies": copies, "launches_per_graph": reps}
 
     for w in SWEEP:
-        if args.only and args.only not in w[0]:
+        if args.only and not any(o in w[0] for o in args.only.split(",")):
             continue
         print(json.dumps(measure(*w)), flush=True)
         torch.cuda.empty_cache()
@@ -624,7 +624,8 @@ def main():
     ap.add_argument("--sweep", action="store_true")
     ap.add_argument("--decode-step", action="store_true",
                     help="config 4: the 64-layer decode-verify step in one CUDA graph, TP = --gpus")
-    ap.add_argument("--only", default="", help="with --sweep/--profile: workloads whose name contains this")
+    ap.add_argument("--only", default="", help="with --sweep: workloads whose name contains one of these comma-separated "
+                         "strings; with --profile: the first workload whose name contains it")
     ap.add_argument("--profile", action="store_true", help="eager launches of one --only workload (for ncu)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

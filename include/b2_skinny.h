@@ -69,11 +69,10 @@ int b2_abi_version(void);
  * kernels/w4.cu:330-334 and the separate w4_reduce_kernel launch (kernels/w4.cu:154-166).
  *
  * Early launch: b2_gemm_f16 and b2_w4_gemm use programmatic dependent launch. Their CTAs may
- * start while the previous GEMM of this library on the stream is still finishing, and stream
- * the first weight tiles (w; qw, qz, sc) into shared memory at once; activations, outputs,
- * workspace and status are touched only after every earlier kernel on the stream has completed.
- * Weights must therefore not be the output of another GEMM of this library on the same stream
- * that may still be running; b2_set_tuning(B2_TUNE_NO_PDL, 1) turns early launch off.
+ * start while the previous kernel of this library on the stream is finishing; until it has
+ * completed they only prefetch their first weight tiles into L2. Every read of operands into
+ * the kernel and every write comes after it has completed, so stream order holds as for a plain
+ * launch. b2_set_tuning(B2_TUNE_NO_PDL, 1) turns early launch off.
  * ---------------------------------------------------------------------------------------- */
 
 /* Bytes of workspace that cover every supported shape on `device` (fixed per device). */

@@ -122,27 +122,41 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// Prefetch the box at (c0, c1) of a 2-D tensor into L2 (no shared memory, no barrier). Safe
+// before griddepcontrol.wait: L2 is where the previous grid's late stores land, so a line
+// fetched early is updated by them, while a copy into shared memory could keep stale data.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(m),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // Loads, stores, barriers
 // ---------------------------------------------------------------------------------------------
-// Not volatile, so the compiler may schedule them among independent arithmetic; the "memory"
-// clobber keeps them after the mbarrier waits (volatile asm with a "memory" clobber), which is
-// what orders them after the TMA writes they read.
+// Volatile with a "memory" clobber: a stage may be read only between the wait on its full
+// barrier and the arrival on its empty barrier, and these loads must stay in that window.
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
-  asm("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-      : "r"(addr)
-      : "memory");
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
   return v;
 }
 __device__ __forceinline__ uint4 ldg_nc128(const void* p) {
   uint4 v;
-  asm("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
-      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-      : "l"(p)
-      : "memory");
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
+}
+// Orders this thread's earlier shared-memory accesses (generic proxy) before later accesses by
+// the async proxy (TMA). A consumer issues it after its last read of a stage and before it
+// releases the stage, whose next TMA fill must not land under those reads.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 // Named barrier over the first `threads` threads of the CTA (the consumer warps).
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {

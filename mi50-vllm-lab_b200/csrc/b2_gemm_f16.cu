@@ -79,12 +79,18 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
   grid_dep_launch();
 
   // ------------------------------------------------------------------ producer warp (1 thread)
-  // The weights never come from the previous grid on the stream, so the producer streams them
-  // without waiting for it (programmatic dependent launch); the consumers wait before they
-  // read x or touch the workspace and y.
+  // Programmatic dependent launch: until the previous grid on the stream has completed, its
+  // stores may not be visible, so the producer only warms L2 with the first stages' weights
+  // before it waits; every load into shared memory comes after.
   if (warp == kWarps) {
     if (lane == 0) {
       tma_prefetch_desc(&tm_w);
+      {
+        UnitCursor cp(sk, u_lo, u_hi);
+        for (int j = 0; j < kStages && cp.left > 0; ++j, cp.next(sk))
+          tma_prefetch_l2_2d(&tm_w, cp.ku * kUnitK, cp.tile * kTileN);
+      }
+      grid_dep_wait();
       const uint64_t pol = l2_evict_first_policy();
       int st = 0;
       uint32_t ph = 0;
@@ -108,10 +114,7 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
         while (!mbar_test(&full[s], last_ph[s]) && globaltimer_ns() - t0 < kPipeWaitNs) {
         }
       }
-      if (*s_abort) {
-        grid_dep_wait();
-        atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
-      }
+      if (*s_abort) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
     }
     return;
   }
@@ -141,6 +144,9 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
       xv[h] = (has_row && k < p.K) ? ldg_nc128(xrow + k) : make_uint4(0, 0, 0, 0);
     }
     if (ok) ok = mbar_wait(&full[st], ph, s_abort);
+    // The lanes poll the barrier one by one and the activation loads above branch on the row,
+    // so the warp may be diverged here; mma.sync.aligned needs all 32 lanes converged.
+    __syncwarp();
     const uint32_t sb = smem_u32(smem + st * kStageBytes);
 #pragma unroll
     for (int T = 0; T < 2; ++T) {
@@ -154,6 +160,7 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
         mma_16816(acc[T][h], a.z, b.z, a.w, b.w, xv[h].z, xv[h].w);
       }
     }
+    fence_proxy_async_smem();  // this lane's reads of the stage precede its next TMA fill
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     if (++st == kStages) st = 0, ph ^= 1u;
@@ -184,31 +191,32 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
         const int r = warp * 32 + T * 16 + g + (i >> 1) * 8;
         if (m < p.M) __stcg(&slot[m * kTileN + r], v[T][i]);
       }
-    // one release by one thread after the barrier covers the whole CTA's stores
+    // every writer makes its partials visible device-wide before the barrier; then one thread
+    // counts the CTA's arrival
+    __threadfence();
     named_bar_sync(1, kWarps * 32);
     if (threadIdx.x == 0) {
-      __threadfence();
       const int prev = atomicAdd(&p.counters[tile], 1);
       const int fin = (prev == last - first);
       if (fin) {
-        atomicExch(&p.counters[tile], 0);
-        __threadfence();
+        p.counters[tile] = 0;  // next used by a later launch, which the kernel boundary orders
+        __threadfence();       // acquire side: the contributors' partials are read after this
       }
       *s_flag = fin;
     }
     named_bar_sync(1, kWarps * 32);
     if (!*s_flag) continue;
-    // add the contributors' slots in CTA order, two contributors' loads in flight at a time
+    // add the contributors' slots in CTA order, eight contributors' loads in flight at a time
     float s[2][4];
 #pragma unroll
     for (int T = 0; T < 2; ++T)
 #pragma unroll
       for (int i = 0; i < 4; ++i) s[T][i] = 0.f;
     const int first_slot = sk_slot_from_begin(sk_begin(sk, first), ts);
-    for (int c0 = first; c0 <= last; c0 += 2) {
-      float a[2][2][4];
+    for (int c0 = first; c0 <= last; c0 += 8) {
+      float a[8][2][4];
 #pragma unroll
-      for (int b = 0; b < 2; ++b) {
+      for (int b = 0; b < 8; ++b) {
         const int c = c0 + b;
         const float* sl = p.partials + ((size_t)c * 2 + (c == first ? first_slot : 0)) * kSlotFloats;
 #pragma unroll
@@ -221,7 +229,7 @@ __global__ void __launch_bounds__(kThreads) gemm_f16_kernel(const __grid_constan
           }
       }
 #pragma unroll
-      for (int b = 0; b < 2; ++b)
+      for (int b = 0; b < 8; ++b)
         if (c0 + b <= last)
 #pragma unroll
           for (int T = 0; T < 2; ++T)

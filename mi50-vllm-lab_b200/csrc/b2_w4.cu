@@ -18,8 +18,9 @@
 //   - stream-K over a persistent grid; tiles shared by CTAs are summed by the last CTA to
 //     finish, in CTA order, from fp32 slots (one launch; replaces the workspace + second
 //     reduce kernel of kernels/w4.cu:154-166,330-346).
-//   - programmatic dependent launch: the first weight stages are requested before the kernel
-//     waits for the previous grid on the stream; activations, workspace and y come after.
+//   - programmatic dependent launch: the first weight stages are prefetched into L2 before the
+//     kernel waits for the previous grid on the stream; every load into shared memory and every
+//     access to activations, workspace and y comes after that wait.
 //   - optionally the NVLink all-reduce of a row-parallel layer is fused into the epilogue: the
 //     finished fp32 tile is pushed to every rank, and each rank adds the ranks' tiles in rank
 //     order (bit-identical on every rank).
@@ -195,16 +196,25 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
         tma_load_2d(s_x + st * C::kXBytes, &tm_x, &full[st], c.ku * kUnitK, 0, pol_x);
         tma_load_2d(s_x + st * C::kXBytes + 1024, &tm_x, &full[st], c.ku * kUnitK + 64, 0, pol_x);
       };
-      // Weights never come from the previous grid on the stream: request the first stages
-      // before waiting for it; their activations follow once it has completed.
+      // Until the previous grid on the stream has completed, its stores may not be visible:
+      // only warm L2 with the first stages' weights, then wait, then load.
       const UnitCursor c0(sk, u_lo, u_hi);
+      {
+        UnitCursor cp = c0;
+        for (int j = 0; j < kStages && cp.left > 0; ++j, cp.next(sk)) {
+          const int n0 = cp.tile * kTileN, grow = (cp.ku * kUnitK) / p.G;
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w) tma_prefetch_l2_2d(&tm_qw, n0 + 32 * w, cp.ku * 16);
+          tma_prefetch_l2_2d(&tm_sc, n0, grow);
+          tma_prefetch_l2_2d(&tm_qz, n0 / 8, grow);
+        }
+      }
+      grid_dep_wait();
       UnitCursor c = c0;
       int issued = 0;
-      for (; issued < kStages && c.left > 0; ++issued, c.next(sk)) issue_w(issued, c);
-      grid_dep_wait();
-      {
-        UnitCursor cx = c0;
-        for (int j = 0; j < issued; ++j, cx.next(sk)) issue_x(j, cx);
+      for (; issued < kStages && c.left > 0; ++issued, c.next(sk)) {
+        issue_w(issued, c);
+        issue_x(issued, c);
       }
       int st = 0;
       uint32_t ph = 0;  // parity of the consumers' release of the unit kStages back
@@ -250,6 +260,9 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
   for (UnitCursor cu(sk, u_lo, u_hi); cu.left > 0; cu.next(sk)) {
     const int tile = cu.tile;
     if (ok) ok = mbar_wait(&full[st], ph, s_abort);
+    // The lanes poll the barrier one by one, so the warp may be diverged here;
+    // mma.sync.aligned needs all 32 lanes converged.
+    __syncwarp();
 
     // activations: lane (g, t) takes chunk 4q + t of row g (box q / 2), the k of its A chunk
     const uint32_t xb = smem_u32(s_x + st * C::kXBytes) + g * 128;
@@ -307,6 +320,7 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
           }
       }
     }
+    fence_proxy_async_smem();  // this lane's reads of the stage precede its next TMA fill
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     if (++st == kStages) st = 0, ph ^= 1u;
@@ -331,28 +345,29 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
       for (int j = 0; j < 2; ++j)
         if (2 * t + j < p.M)
           __stcg(reinterpret_cast<float4*>(slot + (2 * t + j) * kTileN + colw), v[j]);
-      // one release by one thread after the barrier covers the whole CTA's stores
+      // every writer makes its partials visible device-wide before the barrier; then one
+      // thread counts the CTA's arrival
+      __threadfence();
       named_bar_sync(1, kWarps * 32);
       if (threadIdx.x == 0) {
-        __threadfence();
         const int prev = atomicAdd(&p.counters[tile], 1);
         const int fin = (prev == last - first);
         if (fin) {
-          atomicExch(&p.counters[tile], 0);
-          __threadfence();
+          p.counters[tile] = 0;  // next used by a later launch, which the kernel boundary orders
+          __threadfence();       // acquire side: the contributors' partials are read after this
         }
         *s_flag = fin;
       }
       named_bar_sync(1, kWarps * 32);
       finisher = *s_flag != 0;
       if (finisher) {
-        // add the contributors' slots in CTA order, four loads in flight at a time
+        // add the contributors' slots in CTA order, eight loads in flight at a time
         v[0] = v[1] = make_float4(0.f, 0.f, 0.f, 0.f);
         const int first_slot = sk_slot_from_begin(sk_begin(sk, first), ts);
-        for (int c0 = first; c0 <= last; c0 += 4) {
-          float4 a[4][2];
+        for (int c0 = first; c0 <= last; c0 += 8) {
+          float4 a[8][2];
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
+          for (int b = 0; b < 8; ++b) {
             const int c = c0 + b;
             const float* sl =
                 p.partials + ((size_t)c * 2 + (c == first ? first_slot : 0)) * kSlotFloats;
@@ -363,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
                             : make_float4(0.f, 0.f, 0.f, 0.f);
           }
 #pragma unroll
-          for (int b = 0; b < 4; ++b)
+          for (int b = 0; b < 8; ++b)
             if (c0 + b <= last)
 #pragma unroll
               for (int j = 0; j < 2; ++j) {

@@ -21,6 +21,21 @@ def check(y: torch.Tensor, ref: np.ndarray, what: str = "") -> dict:
     return st
 
 
+def mismatch(a: torch.Tensor, b: torch.Tensor, tile: int = 128) -> str:
+    """Where two results of the same call differ: element count, rows, 128-column tiles, the
+    columns inside a tile, and the largest difference (for the message of a failed assert)."""
+    d = a != b
+    if not bool(d.any()):
+        return "equal"
+    idx = d.nonzero()
+    cols = idx[:, 1].unique()
+    big = float((a.float() - b.float()).abs().nan_to_num(float("inf")).max())
+    return (f"{int(d.sum())} elements differ; rows {idx[:, 0].unique().tolist()}; "
+            f"tiles {sorted(set((cols // tile).tolist()))[:16]}; "
+            f"columns in tile {sorted(set((cols % tile).tolist()))[:16]}; max |diff| {big}; "
+            f"nan {int(torch.isnan(a).sum())}/{int(torch.isnan(b).sum())}")
+
+
 def sample_columns(N: int, n: int, seed: int, tile: int = 128) -> np.ndarray:
     """Sorted columns: `n` random ones plus both edges of every 16th tile and the last column."""
     rng = np.random.default_rng(seed)

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from conftest import GOLDEN
-from gpu_util import check, dev, f16_ref_sampled, sample_columns, stream_ptr, workspace
+from gpu_util import check, dev, f16_ref_sampled, mismatch, sample_columns, stream_ptr, workspace
 
 pytestmark = pytest.mark.gpu
 
@@ -41,8 +41,26 @@ def test_config1_lm_head_sampled_columns(ops):
     cols = sample_columns(N, 1500, seed=5)
     check(y[:, torch.from_numpy(cols).cuda()], f16_ref_sampled(x, w, cols), "config 1")
     y2 = ops.gemm(x, w, 20)
-    assert torch.equal(y, y2), "not deterministic"
+    assert torch.equal(y, y2), f"not deterministic: {mismatch(y, y2)}"
     del w
+
+
+def test_weights_written_by_the_previous_kernel(ops):
+    """Weights produced by the kernel launched just before the GEMM (no host sync in between)
+    are read in full: the early start of the GEMM's CTAs must not read them before that
+    kernel's stores have landed. Every call is compared with a repeat made after a sync."""
+    g = torch.Generator(device="cuda").manual_seed(7)
+    M, K, N = 8, 5120, 16384
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    base = torch.randn(N, K, device="cuda", generator=g)
+    outs = []
+    for i in range(8):
+        w = (base * (0.02 + 0.001 * i)).half()  # the kernel right before the GEMM writes w
+        outs.append((ops.gemm(x, w, 0), w))
+    torch.cuda.synchronize()
+    for i, (y, w) in enumerate(outs):
+        y_again = ops.gemm(x, w, 0)
+        assert torch.equal(y, y_again), f"call {i}: {mismatch(y, y_again)}"
 
 
 def test_capi_nan_prefilled_output(capi, oracle):

@@ -8,8 +8,8 @@ import pytest
 import torch
 
 from conftest import GOLDEN
-from gpu_util import (check, dev, sample_columns, stream_ptr, w4_device_inputs, w4_ref_sampled,
-                      workspace)
+from gpu_util import (check, dev, mismatch, sample_columns, stream_ptr, w4_device_inputs,
+                      w4_ref_sampled, workspace)
 
 pytestmark = pytest.mark.gpu
 
@@ -81,6 +81,21 @@ def test_config2_layers_sampled(ops, layer, M):
     cols = sample_columns(N, 300, seed=M)
     check(y[:, torch.from_numpy(cols).cuda()], w4_ref_sampled(x, qw, qz, sc, cols), layer)
     assert torch.equal(y, run(ops, x, qw, qz, sc)), "not deterministic"
+
+
+def test_weights_written_by_the_previous_kernel(ops):
+    """Packed weights produced by the kernel launched just before the GEMM (no host sync in
+    between) are read in full; every call is compared with a repeat made after a sync."""
+    M, K, N = 8, 5120, 8192
+    x, qw, qz, sc = w4_device_inputs(M, K, N, 128, seed=11)
+    outs = []
+    for i in range(8):
+        qwi = qw ^ (0x11111111 * i)  # the kernel right before the GEMM writes the weights
+        outs.append((run(ops, x, qwi, qz, sc), qwi))
+    torch.cuda.synchronize()
+    for i, (y, qwi) in enumerate(outs):
+        y_again = run(ops, x, qwi, qz, sc)
+        assert torch.equal(y, y_again), f"call {i}: {mismatch(y, y_again)}"
 
 
 @pytest.mark.parametrize("P", [2, 4, 8])
