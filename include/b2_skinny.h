@@ -201,6 +201,10 @@ int b2_nvar_destroy(b2_nvar* ar);
 #define B2_TUNE_MIN_UNITS 2       /* fewest k-units per CTA before the grid shrinks (0 = auto)  */
 #define B2_TUNE_NO_PDL 3          /* nonzero: launch every kernel only after the previous one has
                                      finished (no programmatic dependent launch)                 */
+#define B2_TUNE_W4_PATH 4         /* W4 split-K: 0 = choose per shape, 1 = stream-K with a global
+                                     fix-up, 2 = thread-block clusters reducing through
+                                     distributed shared memory                                   */
+#define B2_TUNE_W4_CLUSTER 5      /* cluster path: CTAs per cluster (0 = chosen per shape)      */
 int b2_set_tuning(int key, int value);
 int b2_get_tuning(int key);
 

@@ -73,4 +73,27 @@ int launch_kernel(void (*kernel)(KArgs...), int grid, int block, size_t smem, cu
   return B2_OK;
 }
 
+// The same as a launch of thread-block clusters of `cluster` CTAs along x (grid % cluster == 0).
+template <typename... KArgs, typename... Args>
+int launch_kernel_clusters(void (*kernel)(KArgs...), int grid, int cluster, int block, size_t smem,
+                           cudaStream_t stream, bool early, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (early && tuning(B2_TUNE_NO_PDL) == 0) ? 2 : 1;
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+
 }  // namespace b2

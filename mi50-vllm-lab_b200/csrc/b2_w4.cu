@@ -27,6 +27,8 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "b2_device.cuh"
@@ -83,6 +85,7 @@ struct W4Args {
   float* partials;
   int* counters;
   int* status;
+  int cl_size, cl_count;  // cluster kernel: CTAs per cluster, clusters
 };
 
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t b, uint32_t c) {
@@ -442,11 +445,425 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
   }
 }
 
+// =================================================================================================
+// Cluster split-K variant. The CTAs of one thread-block cluster share output tiles: cluster c
+// owns tiles c, c + NC, ... and CTA rank r of the cluster computes k-units
+// [r * upt / CS, (r + 1) * upt / CS) of each. A tile's partial sums are reduced through
+// distributed shared memory: every CTA leaves its fp32 partial tile in its own shared memory,
+// and CTA r adds column slice r of all CS partials in rank order (deterministic) and writes it.
+// No workspace, no global atomics, no second pass; the fused all-reduce pushes each slice.
+// =================================================================================================
+template <int GP>
+struct CfgC {
+  static constexpr int kStages = 4;  // 4 stages + a 4 KB reduction buffer: four CTAs per SM
+  static constexpr int RG = 4 / GP;
+  static constexpr int kScBytes = RG * kTileN * 2;
+  static constexpr int kQzBytes = RG * (kTileN / 8) * 4;
+  static constexpr int kScStride = align128(kScBytes);
+  static constexpr int kQzStride = align128(kQzBytes);
+  static constexpr int kXBytes = kMaxM * kUnitK * 2;
+  static constexpr int kTx = kQwStage + kXBytes + kScBytes + kQzBytes;
+  static constexpr int kXOff = kStages * kQwStage;
+  static constexpr int kScOff = kXOff + kStages * kXBytes;
+  static constexpr int kQzOff = kScOff + kStages * kScStride;
+  static constexpr int kRedOff = kQzOff + kStages * kQzStride;  // [8 rows][128 columns] fp32
+  static constexpr int kBarOff = kRedOff + kMaxM * kTileN * 4;
+  static constexpr int kSmem = 1024 + kBarOff + (2 * kStages + 2) * 8 + 32;
+  static_assert(kXOff % 1024 == 0 && kXBytes % 1024 == 0, "swizzled boxes need 1024 B");
+  static_assert(kScOff % 128 == 0 && kQzOff % 128 == 0 && kRedOff % 128 == 0, "alignment");
+};
+
+template <int GP, bool FUSED>
+__global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
+    w4c_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_sc,
+               const __grid_constant__ CUtensorMap tm_qz, const __grid_constant__ CUtensorMap tm_x,
+               const W4Args p, const ArView ar) {
+  using C = CfgC<GP>;
+  constexpr int RG = C::RG;
+  constexpr int kStages = C::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* s_qw = smem;
+  uint8_t* s_x = smem + C::kXOff;
+  uint8_t* s_sc = smem + C::kScOff;
+  uint8_t* s_qz = smem + C::kQzOff;
+  float* s_red = reinterpret_cast<float*>(smem + C::kRedOff);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* empty = full + kStages;
+  uint64_t* red_full = empty + kStages;  // every CTA of the cluster left its partial tile
+  uint64_t* red_empty = red_full + 1;    // every CTA of the cluster finished reading mine
+  volatile int* s_abort = reinterpret_cast<volatile int*>(red_empty + 1);
+  volatile int* s_flag = s_abort + 1;
+  volatile uint32_t* s_gen = reinterpret_cast<volatile uint32_t*>(s_abort + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int CS = p.cl_size, NC = p.cl_count;
+  const int crank = (int)cluster_ctarank();
+  const int cid = blockIdx.x / CS;
+  const int upt = p.sk.upt, tiles = p.sk.tiles;
+  const int k0 = upt * crank / CS, k1 = upt * (crank + 1) / CS, nk = k1 - k0;
+  const int ntile = (tiles - 1 - cid) / NC + 1;
+  const int n_units = ntile * nk;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kWarps);
+    }
+    mbar_init(red_full, CS);
+    mbar_init(red_empty, CS);
+    *s_abort = 0;
+    *s_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  cluster_sync_all();  // no CTA arrives on a peer's barrier before the peer initialised it
+  grid_dep_launch();
+
+  // ------------------------------------------------------------------ producer warp (1 thread)
+  if (warp == kWarps) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_qw);
+      tma_prefetch_desc(&tm_sc);
+      tma_prefetch_desc(&tm_qz);
+      tma_prefetch_desc(&tm_x);
+      const uint64_t pol_w = l2_evict_first_policy();
+      const uint64_t pol_x = l2_evict_normal_policy();
+      // unit j of this CTA: tile cid + (j / nk) * NC, k-unit k0 + j % nk
+      auto where = [&](int j, int& tile, int& ku) {
+        const int i = j / nk;
+        tile = cid + i * NC;
+        ku = k0 + (j - i * nk);
+      };
+      auto issue = [&](int st, int j, bool with_w, bool with_x) {
+        int tile, ku;
+        where(j, tile, ku);
+        const int n0 = tile * kTileN;
+        if (with_w) {
+          const int grow = (ku * kUnitK) / p.G;
+          mbar_arrive_expect_tx(&full[st], C::kTx);
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w)
+            tma_load_2d(s_qw + st * kQwStage + w * kQwBox, &tm_qw, &full[st], n0 + 32 * w, ku * 16,
+                        pol_w);
+          tma_load_2d(s_sc + st * C::kScStride, &tm_sc, &full[st], n0, grow, pol_w);
+          tma_load_2d(s_qz + st * C::kQzStride, &tm_qz, &full[st], n0 / 8, grow, pol_w);
+        }
+        if (with_x) {
+          tma_load_2d(s_x + st * C::kXBytes, &tm_x, &full[st], ku * kUnitK, 0, pol_x);
+          tma_load_2d(s_x + st * C::kXBytes + 1024, &tm_x, &full[st], ku * kUnitK + 64, 0, pol_x);
+        }
+      };
+      // until the previous grid has completed only warm L2 with the first stages' weights
+      for (int j = 0; j < kStages && j < n_units; ++j) {
+        int tile, ku;
+        where(j, tile, ku);
+        const int n0 = tile * kTileN, grow = (ku * kUnitK) / p.G;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) tma_prefetch_l2_2d(&tm_qw, n0 + 32 * w, ku * 16);
+        tma_prefetch_l2_2d(&tm_sc, n0, grow);
+        tma_prefetch_l2_2d(&tm_qz, n0 / 8, grow);
+      }
+      grid_dep_wait();
+      int issued = 0;
+      for (; issued < kStages && issued < n_units; ++issued) issue(issued, issued, true, true);
+      int st = 0;
+      uint32_t ph = 0;
+      for (; issued < n_units; ++issued) {
+        if (!mbar_wait_backoff(&empty[st], ph, s_abort)) break;
+        issue(st, issued, true, true);
+        if (++st == kStages) st = 0, ph ^= 1u;
+      }
+      for (int s = 0; s < kStages && s < issued; ++s) {
+        const int u = s + ((issued - 1 - s) / kStages) * kStages;
+        const uint32_t par = (uint32_t)((u / kStages) & 1);
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_test(&full[s], par) && globaltimer_ns() - t0 < kPipeWaitNs) {
+        }
+      }
+      if (*s_abort) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumer warps
+  grid_dep_wait();
+  if (FUSED && threadIdx.x == 0) *s_gen = ar_begin(ar);
+  named_bar_sync(1, kWarps * 32);
+  const int g = lane >> 2, t = lane & 3;
+  const int ch = ((g & 1) << 2) | (g >> 1);
+  const int colw = warp * 32 + ch * 4;
+  const uint32_t e = FUSED ? *s_gen : 0u;
+  const int tid = threadIdx.x;
+  // column slice of every tile that this CTA reduces and writes
+  const int c0 = kTileN * crank / CS, c1 = kTileN * (crank + 1) / CS, W = c1 - c0;
+  const uint32_t red_addr = smem_u32(s_red);
+
+  float acc[2][4], accg[2][4];
+#pragma unroll
+  for (int T = 0; T < 2; ++T)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[T][i] = accg[T][i] = 0.f;
+
+  int st = 0;
+  uint32_t ph = 0;
+  bool ok = true;
+  for (int it = 0; it < ntile; ++it) {
+    const int tile = cid + it * NC;
+    for (int ku = k0; ku < k1; ++ku) {
+      if (ok) ok = mbar_wait(&full[st], ph, s_abort);
+      __syncwarp();
+      const uint32_t xb = smem_u32(s_x + st * C::kXBytes) + g * 128;
+      uint4 xv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        xv[q] = lds128(xb + (q >> 1) * 1024 + ((((4 * q + t) & 7) ^ g) << 4));
+      uint32_t zlo[RG][4], zhi[RG][4];
+      float scl[RG][4];
+#pragma unroll
+      for (int r = 0; r < RG; ++r) {
+        const uint32_t* qz_row =
+            reinterpret_cast<const uint32_t*>(s_qz + st * C::kQzStride) + r * (kTileN / 8);
+        const __half* sc_row = reinterpret_cast<const __half*>(s_sc + st * C::kScStride) + r * kTileN;
+        const uint32_t zw = qz_row[colw >> 3] >> ((colw & 7) * 4);
+        const uint2 sv = *reinterpret_cast<const uint2*>(sc_row + colw);
+        const __half2 s01 = *reinterpret_cast<const __half2*>(&sv.x);
+        const __half2 s23 = *reinterpret_cast<const __half2*>(&sv.y);
+        scl[r][0] = __low2float(s01);
+        scl[r][1] = __high2float(s01);
+        scl[r][2] = __low2float(s23);
+        scl[r][3] = __high2float(s23);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t z = (zw >> (4 * i)) & 0xFu;
+          zlo[r][i] = (0xE400u + z) * 0x00010001u;
+          zhi[r][i] = (0xD400u + (z << 4)) * 0x00010001u;
+        }
+      }
+      const uint32_t qb = smem_u32(s_qw + st * kQwStage + warp * kQwBox);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int row = 4 * q + t;
+        const uint4 w = lds128(qb + row * 128 + ((ch ^ (row & 7)) << 4));
+        const int r = (RG == 1) ? 0 : (q / GP);
+        uint32_t d0[4], d1[4], d2[4], d3[4];
+        dequant_word(w.x, zlo[r][0], zhi[r][0], d0);
+        dequant_word(w.y, zlo[r][1], zhi[r][1], d1);
+        dequant_word(w.z, zlo[r][2], zhi[r][2], d2);
+        dequant_word(w.w, zlo[r][3], zhi[r][3], d3);
+        mma_16816(accg[0], d0[0], d1[0], d0[1], d1[1], xv[q].x, xv[q].y);
+        mma_16816(accg[0], d0[2], d1[2], d0[3], d1[3], xv[q].z, xv[q].w);
+        mma_16816(accg[1], d2[0], d3[0], d2[1], d3[1], xv[q].x, xv[q].y);
+        mma_16816(accg[1], d2[2], d3[2], d2[3], d3[3], xv[q].z, xv[q].w);
+        if ((q + 1) % GP == 0) {
+#pragma unroll
+          for (int T = 0; T < 2; ++T)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              acc[T][i] = fmaf(scl[r][2 * T + (i >> 1)], accg[T][i], acc[T][i]);
+              accg[T][i] = 0.f;
+            }
+        }
+      }
+      fence_proxy_async_smem();  // this lane's reads of the stage precede its next TMA fill
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (++st == kStages) st = 0, ph ^= 1u;
+    }
+
+    // ---------------------------------------------------------------- tile epilogue: reduce
+    // my partial tile -> my reduction buffer, once every CTA has read the previous one. One
+    // thread waits; the CTA barrier orders the other threads after its acquire (and, further
+    // down, their writes before its release-arrive), as the PTX memory model's causality order
+    // composes the two.
+    if (it > 0) {
+      if (tid == 0) *s_flag = mbar_wait_cluster(red_empty, (uint32_t)((it - 1) & 1), s_abort);
+      named_bar_sync(1, kWarps * 32);
+      ok = ok && *s_flag;
+    }
+    {
+      const float4 v0 = make_float4(acc[0][0], acc[0][2], acc[1][0], acc[1][2]);  // m = 2t
+      const float4 v1 = make_float4(acc[0][1], acc[0][3], acc[1][1], acc[1][3]);  // m = 2t + 1
+      if (2 * t < p.M) *reinterpret_cast<float4*>(s_red + (2 * t) * kTileN + colw) = v0;
+      if (2 * t + 1 < p.M) *reinterpret_cast<float4*>(s_red + (2 * t + 1) * kTileN + colw) = v1;
+    }
+#pragma unroll
+    for (int T = 0; T < 2; ++T)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[T][i] = 0.f;
+    named_bar_sync(1, kWarps * 32);
+    // lane q tells CTA q (one release-arrive each, issued together by warp 0)
+    if (tid < CS) mbar_arrive_remote(mapa_shared(smem_u32(red_full), (uint32_t)tid));
+    if (tid == 0) *s_flag = mbar_wait_cluster(red_full, (uint32_t)(it & 1), s_abort);
+    named_bar_sync(1, kWarps * 32);
+    ok = ok && *s_flag;
+    // slice [c0, c1) of the tile: the CS partials added in rank order
+    for (int idx = tid; idx < p.M * W; idx += kWarps * 32) {
+      const int m = idx / W, col = c0 + (idx - m * W);
+      const uint32_t off = red_addr + (uint32_t)(m * kTileN + col) * 4u;
+      float part[16];  // all CS loads in flight, then the sum in rank order
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        part[q] = (q < CS) ? ld_dsmem_f32(mapa_shared(off, (uint32_t)q)) : 0.f;
+      float s = 0.f;
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        if (q < CS) s += part[q];
+      const int n = tile * kTileN + col;
+      if (n < p.N) {
+        if (!FUSED) {
+          p.y[(size_t)m * p.N + n] = __float2half_rn(s);
+        } else {
+          for (int r = 0; r < ar.world; ++r)
+            reinterpret_cast<float*>(ar_slot(ar, r, e & 1u, ar.rank))[(size_t)m * p.N + n] = s;
+        }
+      }
+    }
+    named_bar_sync(1, kWarps * 32);
+    if (tid < CS) mbar_arrive_remote(mapa_shared(smem_u32(red_empty), (uint32_t)tid));
+    // slice `crank` of the tile is pushed: publish it on every rank (one system-scope release
+    // fence by the publishing thread covers the CTA's stores, ordered by the barrier above)
+    if (FUSED && tid == 0) ar_publish(ar, tile * CS + crank, e);
+  }
+  if constexpr (FUSED) {
+    // -------------------------------------------------------------- fused all-reduce, phase 2
+    for (int it = 0; it < ntile; ++it) {
+      const int tile = cid + it * NC;
+      named_bar_sync(1, kWarps * 32);
+      if (tid == 0) *s_flag = ar_wait(ar, tile * CS + crank, e) ? 1 : 0;
+      named_bar_sync(1, kWarps * 32);
+      __threadfence();
+      for (int idx = tid; idx < p.M * W; idx += kWarps * 32) {
+        const int m = idx / W, col = c0 + (idx - m * W);
+        const int n = tile * kTileN + col;
+        if (n >= p.N) continue;
+        float s = 0.f;
+        for (int src = 0; src < ar.world; ++src)
+          s += __ldcg(reinterpret_cast<const float*>(ar_slot(ar, ar.rank, e & 1u, src)) +
+                      (size_t)m * p.N + n);
+        p.y[(size_t)m * p.N + n] = __float2half_rn(s);
+      }
+    }
+    named_bar_sync(1, kWarps * 32);
+    if (tid == 0) ar_finish(ar, e);
+  }
+  // Nobody may still read my reduction buffer or arrive on my barriers when this CTA exits: the
+  // release of my last tile's buffer is every peer's last access to my shared memory.
+  {
+    // wait the full bound here even after an earlier timeout: exiting while a peer still reads
+    // this CTA's shared memory is worse than waiting
+    volatile int* no_abort = s_flag + 2;  // a zeroed word of its own
+    named_bar_sync(1, kWarps * 32);
+    if (tid == 0) {
+      *no_abort = 0;
+      if (!mbar_wait_cluster(red_empty, (uint32_t)((ntile - 1) & 1), no_abort)) *s_flag = 0;
+    }
+    named_bar_sync(1, kWarps * 32);
+    ok = ok && *s_flag;
+  }
+  if (!ok && lane == 0) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
+}
+
 struct KernelCache {
   bool configured = false;
   int occ = 0;
 };
 KernelCache g_cache[64][3][2];
+
+// The four tensor maps of a launch (weights, scales, zeros, activations).
+template <int RG>
+int encode_maps(const W4Args& a, const void* qw, const void* qz, const void* sc, CUtensorMap* m_qw,
+                CUtensorMap* m_sc, CUtensorMap* m_qz, CUtensorMap* m_x) {
+  const int K = a.K, N = a.N, G = a.G;
+  int rc = encode_2d(m_qw, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, (uint64_t)N, (uint64_t)(K / 8),
+                     (uint64_t)N * 4, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = encode_2d(m_sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, (uint64_t)N, (uint64_t)(K / G),
+                 (uint64_t)N * 2, kTileN, RG, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  rc = encode_2d(m_qz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, (uint64_t)(N / 8), (uint64_t)(K / G),
+                 (uint64_t)N / 2, kTileN / 8, RG, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (rc) return rc;
+  // activations [M rows, K] fp16; rows M..7 of a box read as zeros (out of bounds)
+  return encode_2d(m_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)K, (uint64_t)a.M,
+                   (uint64_t)K * 2, 64, kMaxM, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// B2_LOG_PLAN=1 in the environment prints the split-K plan of every W4 launch to stderr.
+bool plan_log() {
+  static const bool on = [] {
+    const char* v = std::getenv("B2_LOG_PLAN");
+    return v && v[0] && v[0] != '0';
+  }();
+  return on;
+}
+
+// How many clusters of 1..16 CTAs of the cluster kernel can be resident at once (per device).
+struct ClusterCaps {
+  bool configured = false;
+  int max_clusters[17] = {0};
+};
+ClusterCaps g_ccaps[64][3][2];
+
+template <int GP, bool FUSED>
+int cluster_caps(int dev, const ClusterCaps** out) {
+  using C = CfgC<GP>;
+  ClusterCaps& cc = g_ccaps[dev][GP == 1 ? 0 : GP == 2 ? 1 : 2][FUSED ? 1 : 0];
+  if (!cc.configured) {
+    auto kern = w4c_kernel<GP, FUSED>;
+    B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
+    // clusters of more than 8 CTAs are allowed on this part when asked for
+    const bool big = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+                     cudaSuccess;
+    (void)cudaGetLastError();
+    for (int cs = 1; cs <= 16; ++cs) {
+      cc.max_clusters[cs] = 0;
+      if (cs > 8 && !big) continue;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(cs * 64));
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = C::kSmem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = (unsigned)cs;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess) cc.max_clusters[cs] = n;
+      (void)cudaGetLastError();
+    }
+    cc.configured = true;
+  }
+  *out = &cc;
+  return B2_OK;
+}
+
+// Cluster plan for `tiles` output tiles of `upt` k-units: the cluster size with the smallest
+// critical path (tiles per cluster x k-units per CTA, plus half a unit for the shared-memory
+// reduction when the tile is split). Returns the cost in unit-times, or a negative value when no
+// cluster size fits.
+double plan_clusters(const ClusterCaps& cc, int tiles, int upt, int want, int max_cs, int* cs_out,
+                     int* nc_out) {
+  double best = -1.0;
+  for (int cs = 1; cs <= 16 && cs <= upt && cs <= max_cs; ++cs) {
+    if (want > 0 && cs != want) continue;
+    const int ncmax = cc.max_clusters[cs];
+    if (ncmax < 1) continue;
+    const int nc = std::min(tiles, ncmax);
+    const int per_cluster = (tiles + nc - 1) / nc;
+    const int ku = (upt + cs - 1) / cs;
+    const double cost = per_cluster * (ku + (cs > 1 ? 0.5 : 0.0));
+    if (best < 0.0 || cost < best - 1e-9) {
+      best = cost;
+      *cs_out = cs;
+      *nc_out = nc;
+    }
+  }
+  return best;
+}
 
 template <int GP, bool FUSED>
 int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, const ArView* ar,
@@ -466,7 +883,7 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
     if (kc.occ < 1) return fail(B2_ERR_UNSUPPORTED, "w4: kernel does not fit on an SM");
     kc.configured = true;
   }
-  const int K = a.K, N = a.N, G = a.G;
+  const int K = a.K, N = a.N;
   StreamK sk;
   sk.upt = K / kUnitK;
   sk.tiles = (N + kTileN - 1) / kTileN;
@@ -480,21 +897,46 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
   a.sk = sk;
 
   CUtensorMap m_qw, m_sc, m_qz, m_x;
-  rc = encode_2d(&m_qw, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, (uint64_t)N, (uint64_t)(K / 8),
-                 (uint64_t)N * 4, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  rc = encode_2d(&m_sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, (uint64_t)N, (uint64_t)(K / G),
-                 (uint64_t)N * 2, kTileN, C::RG, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc) return rc;
-  rc = encode_2d(&m_qz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, (uint64_t)(N / 8), (uint64_t)(K / G),
-                 (uint64_t)N / 2, kTileN / 8, C::RG, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc) return rc;
-  // activations [M rows, K] fp16; rows M..7 of a box read as zeros (out of bounds)
-  rc = encode_2d(&m_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)K, (uint64_t)a.M,
-                 (uint64_t)K * 2, 64, kMaxM, CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = encode_maps<C::RG>(a, qw, qz, sc, &m_qw, &m_sc, &m_qz, &m_x);
   if (rc) return rc;
   const ArView view = ar ? *ar : ArView{};
-  return launch_kernel(kern, sk.ctas, kThreads, C::kSmem, stream, early && !FUSED, m_qw, m_sc,
+
+  // Split-K path. The scratch-only entry point (max_ctas below the workspace bound) always takes
+  // stream-K, whose fix-up is what its scratch is for.
+  // The fused all-reduce defaults to stream-K: in the cluster kernel every CTA publishes its own
+  // slice (hundreds of system-scope fences and flags per call), which measured slower at TP=2
+  // (down_proj shard: 32-39 us against a 20 us GEMM + separate all-reduce). B2_TUNE_W4_PATH = 2
+  // selects it.
+  const int path = tuning(B2_TUNE_W4_PATH);
+  if (path == 2 || (path == 0 && !FUSED && max_ctas >= kWsMaxCtas)) {
+    const ClusterCaps* cc = nullptr;
+    rc = cluster_caps<GP, FUSED>(dev, &cc);
+    if (rc) return rc;
+    int cs = 0, nc = 0;
+    // the fused all-reduce publishes one flag per (tile, slice)
+    const int max_cs = FUSED ? kArMaxFlags / sk.tiles : 16;
+    const double cost =
+        plan_clusters(*cc, sk.tiles, sk.upt, tuning(B2_TUNE_W4_CLUSTER), max_cs, &cs, &nc);
+    // stream-K: even units per CTA, plus the tail of the CTAs that finish a shared tile
+    const long long per_cta = (sk.total + sk.ctas - 1) / sk.ctas;
+    const double sk_cost = (double)per_cta + ((sk.total % sk.upt == 0 && sk.ctas <= sk.tiles &&
+                                               sk.tiles % sk.ctas == 0) ? 0.0 : 4.0);
+    if (plan_log()) {
+      std::fprintf(stderr, "b2 w4 plan: M=%d K=%d N=%d tiles=%d upt=%d | stream-K ctas=%d cost=%.1f | "
+                   "cluster cs=%d nc=%d cost=%.1f | max clusters:", a.M, K, N, sk.tiles, sk.upt,
+                   sk.ctas, sk_cost, cs, nc, cost);
+      for (int i = 1; i <= 16; ++i) std::fprintf(stderr, " %d", cc->max_clusters[i]);
+      std::fprintf(stderr, "\n");
+    }
+    if (cost > 0.0 && (path == 2 || cost <= sk_cost)) {
+      a.cl_size = cs;
+      a.cl_count = nc;
+      return launch_kernel_clusters(w4c_kernel<GP, FUSED>, nc * cs, cs, kThreads, CfgC<GP>::kSmem,
+                                    stream, early, m_qw, m_sc, m_qz, m_x, a, view);
+    }
+  }
+  a.cl_size = a.cl_count = 0;
+  return launch_kernel(kern, sk.ctas, kThreads, C::kSmem, stream, early, m_qw, m_sc,
                        m_qz, m_x, a, view);
 }
 
@@ -545,8 +987,8 @@ W4Args make_args(const void* a, void* y, int M, int K, int N, int G, void* ws) {
   return r;
 }
 
-// `early`: programmatic dependent launch (the plain GEMM only; the fused all-reduce and the
-// no-alloc variant, which clears its scratch with a memset just before, launch normally).
+// `early`: programmatic dependent launch (the no-alloc variant, which clears its scratch with a
+// memset just before, launches normally).
 template <bool FUSED>
 int dispatch(const W4Args& args, const void* qw, const void* qz, const void* sc, const ArView* ar,
              cudaStream_t stream, int max_ctas = kWsMaxCtas, bool early = false) {
@@ -643,7 +1085,11 @@ int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* q
   if (rc) return rc;
   if ((N + kTileN - 1) / kTileN > tiles_cap)
     return fail(B2_ERR_INVALID_ARG, "w4_allreduce: N=%d has more tiles than flags", N);
-  return dispatch<true>(make_args(a, y, M, K, N, G, ws), qw, qz, sc, &v, stream);
+  // Early launch is safe here too: the generation is read after griddepcontrol.wait, and a
+  // dependent grid starts only once every CTA of this one is resident, so none of the CTAs that
+  // wait for peers in the second phase can be held back.
+  return dispatch<true>(make_args(a, y, M, K, N, G, ws), qw, qz, sc, &v, stream, kWsMaxCtas,
+                        /*early=*/true);
 }
 
 }  // namespace b2
