@@ -195,7 +195,8 @@ int b2_nvar_world(const b2_nvar* ar);
 int b2_nvar_destroy(b2_nvar* ar);
 
 /* ------------------------------------------------------------------------------------------
- * Tuning (process-wide; for measurement sweeps)
+ * Tuning (process-wide; for measurement sweeps). B2_TUNE="key=value,..." in the environment
+ * presets keys before first use; b2_set_tuning overrides them.
  * ---------------------------------------------------------------------------------------- */
 #define B2_TUNE_CTAS_PER_SM 1     /* resident CTAs per SM the stream-K grid targets (0 = auto) */
 #define B2_TUNE_MIN_UNITS 2       /* fewest k-units per CTA before the grid shrinks (0 = auto)  */

@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 
 #include "b2_device.cuh"
@@ -169,7 +170,32 @@ size_t ws_total_bytes() {
 // ----------------------------------------------------------------------------------------------
 static std::atomic<int> g_tune[8];
 
-int tuning(int key) { return (key >= 0 && key < 8) ? g_tune[key].load() : 0; }
+// B2_TUNE="key=value,key=value" in the environment presets tuning keys (read once, before the
+// first use; b2_set_tuning overrides).
+static void tuning_from_env() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    const char* env = std::getenv("B2_TUNE");
+    if (!env) return;
+    const char* p = env;
+    while (*p) {
+      char* end = nullptr;
+      const long k = std::strtol(p, &end, 10);
+      if (end == p || *end != '=') break;
+      p = end + 1;
+      const long v = std::strtol(p, &end, 10);
+      if (end == p) break;
+      if (k >= 0 && k < 8) g_tune[k].store((int)v);
+      p = end;
+      if (*p == ',') ++p;
+    }
+  });
+}
+
+int tuning(int key) {
+  tuning_from_env();
+  return (key >= 0 && key < 8) ? g_tune[key].load() : 0;
+}
 
 int streamk_ctas(long long total, int sm_count, int occ, int min_units_default) {
   int cps = tuning(B2_TUNE_CTAS_PER_SM);
@@ -230,6 +256,7 @@ int b2_workspace_status(void* ws, int clear, int* device_status) {
 }
 
 int b2_set_tuning(int key, int value) {
+  tuning_from_env();
   if (key < 0 || key >= 8) return fail(B2_ERR_INVALID_ARG, "unknown tuning key %d", key);
   g_tune[key].store(value);
   return B2_OK;

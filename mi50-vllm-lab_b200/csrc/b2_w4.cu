@@ -715,33 +715,40 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
         if (!FUSED) {
           p.y[(size_t)m * p.N + n] = __float2half_rn(s);
         } else {
+          // exchange layout: slice (tile, crank) is one block of M x W floats at
+          // (tile * 128 + c0) * M, element idx in the order the threads produce them, so a
+          // warp's pushes over NVLink are coalesced (needs N % 128 == 0, checked on the host)
+          const size_t at = ((size_t)tile * kTileN + c0) * p.M + idx;
           for (int r = 0; r < ar.world; ++r)
-            reinterpret_cast<float*>(ar_slot(ar, r, e & 1u, ar.rank))[(size_t)m * p.N + n] = s;
+            reinterpret_cast<float*>(ar_slot(ar, r, e & 1u, ar.rank))[at] = s;
         }
       }
     }
     named_bar_sync(1, kWarps * 32);
     if (tid < CS) mbar_arrive_remote(mapa_shared(smem_u32(red_empty), (uint32_t)tid));
-    // slice `crank` of the tile is pushed: publish it on every rank (one system-scope release
-    // fence by the publishing thread covers the CTA's stores, ordered by the barrier above)
-    if (FUSED && tid == 0) ar_publish(ar, tile * CS + crank, e);
+    // Every CTA of the cluster has pushed its slice once CTA 0's buffer release completes: CTA 0
+    // publishes the tile with one system-scope fence (the peers' pushes happen before it through
+    // their CTA barrier and cluster-scope release, which the fence's cumulativity covers).
+    if (FUSED && crank == 0 && tid == 0) {
+      if (mbar_wait_cluster(red_empty, (uint32_t)(it & 1), s_abort)) ar_publish(ar, tile, e);
+    }
   }
   if constexpr (FUSED) {
     // -------------------------------------------------------------- fused all-reduce, phase 2
     for (int it = 0; it < ntile; ++it) {
       const int tile = cid + it * NC;
       named_bar_sync(1, kWarps * 32);
-      if (tid == 0) *s_flag = ar_wait(ar, tile * CS + crank, e) ? 1 : 0;
+      if (tid == 0) *s_flag = ar_wait(ar, tile, e) ? 1 : 0;
       named_bar_sync(1, kWarps * 32);
       __threadfence();
+      const size_t blk = ((size_t)tile * kTileN + c0) * p.M;
       for (int idx = tid; idx < p.M * W; idx += kWarps * 32) {
         const int m = idx / W, col = c0 + (idx - m * W);
         const int n = tile * kTileN + col;
         if (n >= p.N) continue;
         float s = 0.f;
         for (int src = 0; src < ar.world; ++src)
-          s += __ldcg(reinterpret_cast<const float*>(ar_slot(ar, ar.rank, e & 1u, src)) +
-                      (size_t)m * p.N + n);
+          s += __ldcg(reinterpret_cast<const float*>(ar_slot(ar, ar.rank, e & 1u, src)) + blk + idx);
         p.y[(size_t)m * p.N + n] = __float2half_rn(s);
       }
     }
@@ -903,18 +910,17 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
 
   // Split-K path. The scratch-only entry point (max_ctas below the workspace bound) always takes
   // stream-K, whose fix-up is what its scratch is for.
-  // The fused all-reduce defaults to stream-K: in the cluster kernel every CTA publishes its own
-  // slice (hundreds of system-scope fences and flags per call), which measured slower at TP=2
-  // (down_proj shard: 32-39 us against a 20 us GEMM + separate all-reduce). B2_TUNE_W4_PATH = 2
-  // selects it.
+  // Fused launches default to stream-K (measured faster at TP=2: 24.9 us against 38.9 us for the
+  // cluster kernel's fused epilogue); B2_TUNE_W4_PATH = 2 selects the cluster kernel, which needs N
+  // to be a whole number of tiles (its exchange blocks then fit the M x N slot exactly).
   const int path = tuning(B2_TUNE_W4_PATH);
-  if (path == 2 || (path == 0 && !FUSED && max_ctas >= kWsMaxCtas)) {
+  const bool cluster_ok = !FUSED || N % kTileN == 0;
+  if (cluster_ok && (path == 2 || (path == 0 && !FUSED && max_ctas >= kWsMaxCtas))) {
     const ClusterCaps* cc = nullptr;
     rc = cluster_caps<GP, FUSED>(dev, &cc);
     if (rc) return rc;
     int cs = 0, nc = 0;
-    // the fused all-reduce publishes one flag per (tile, slice)
-    const int max_cs = FUSED ? kArMaxFlags / sk.tiles : 16;
+    const int max_cs = 16;
     const double cost =
         plan_clusters(*cc, sk.tiles, sk.upt, tuning(B2_TUNE_W4_CLUSTER), max_cs, &cs, &nc);
     // stream-K: even units per CTA, plus the tail of the CTAs that finish a shared tile
