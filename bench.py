@@ -523,7 +523,8 @@ def run_decode_step(args):
         import torch.distributed as dist
 
         cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
-        ar = vllm_shim.NvlinkAllReduce(cpu, rank, list(range(P)), slot_bytes=M * H * 4)
+        # 8 bytes per output element: room for the low-latency (value + generation) exchange
+        ar = vllm_shim.NvlinkAllReduce(cpu, rank, list(range(P)), slot_bytes=M * H * 8)
     g = torch.Generator(device="cuda").manual_seed(4000 + rank)
 
     def w4(K, N):

@@ -81,6 +81,34 @@ __device__ __forceinline__ bool ar_wait(const ArView& v, int idx, uint32_t e) {
   return true;
 }
 
+// Low-latency exchange: a 64-bit word carries an fp32 value in its low half and the generation
+// in its high half, written with one single-copy-atomic 64-bit store, so the reader needs no flag
+// and the writer no fence: a word whose high half equals e holds generation e's value. Slots start
+// zeroed and e >= 1, and a slot parity is reused only at e + 2 (see above), so no stale word ever
+// carries e.
+__device__ __forceinline__ void ll_store(uint64_t* p, float v, uint32_t e) {
+  const uint64_t w = ((uint64_t)e << 32) | (uint64_t)__float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+// Wait (bounded by the absolute globaltimer deadline) for generation e's value at p.
+__device__ __forceinline__ bool ll_load(const uint64_t* p, uint32_t e,
+                                        unsigned long long deadline_ns, float* out) {
+  for (unsigned int it = 0; it < kMaxSpin; ++it) {
+    uint64_t w;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    if ((uint32_t)(w >> 32) == e) {
+      *out = __uint_as_float((uint32_t)w);
+      return true;
+    }
+    if ((it & 15u) == 15u) {
+      if (globaltimer_ns() > deadline_ns) break;
+      __nanosleep(32);
+    }
+  }
+  *out = 0.f;
+  return false;
+}
+
 // Count this CTA as finished; the last CTA of the launch advances the generation. One thread,
 // after the CTA's last use of the buffer.
 __device__ __forceinline__ void ar_finish(const ArView& v, uint32_t e) {

@@ -86,6 +86,7 @@ struct W4Args {
   int* counters;
   int* status;
   int cl_size, cl_count;  // cluster kernel: CTAs per cluster, clusters
+  int ll;                 // fused stream-K: exchange as 64-bit value+generation words
 };
 
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t b, uint32_t c) {
@@ -399,8 +400,25 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
       continue;
     }
     // Fused all-reduce: push this rank's finished fp32 tile into slot[e&1][rank] of every rank
-    // ([M][N] fp32 layout), then publish the tile's flag on every rank.
+    // ([M][N] layout). Low-latency form: 64-bit value+generation words, nothing else to publish.
+    // Otherwise fp32 values, then the tile's flag on every rank.
     const int n = tile * kTileN + colw;
+    if (p.ll) {
+      if (n < p.N)
+        for (int r = 0; r < ar.world; ++r) {
+          uint64_t* dst = reinterpret_cast<uint64_t*>(ar_slot(ar, r, e & 1u, ar.rank));
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            if (2 * t + j < p.M) {
+              uint64_t* d = dst + (size_t)(2 * t + j) * p.N + n;
+              ll_store(d + 0, v[j].x, e);
+              ll_store(d + 1, v[j].y, e);
+              ll_store(d + 2, v[j].z, e);
+              ll_store(d + 3, v[j].w, e);
+            }
+        }
+      continue;
+    }
     if (n < p.N) {
       for (int r = 0; r < ar.world; ++r) {
         float* dst = reinterpret_cast<float*>(ar_slot(ar, r, e & 1u, ar.rank));
@@ -416,12 +434,39 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
   if constexpr (FUSED) {
     // -------------------------------------------------------------- fused all-reduce, phase 2
     // CTA b adds tiles b, b + grid, ... over all ranks in rank order and writes the fp16 result.
+    const unsigned long long deadline = globaltimer_ns() + ar.timeout_ns;
     for (int tile = blockIdx.x; tile < sk.tiles; tile += gridDim.x) {
+      const int n = tile * kTileN + colw;
+      if (p.ll) {
+        if (n >= p.N) continue;
+        float4 v[2];
+        v[0] = v[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        bool got = true;
+        for (int src = 0; src < ar.world; ++src) {
+          const uint64_t* sl = reinterpret_cast<const uint64_t*>(ar_slot(ar, ar.rank, e & 1u, src));
+#pragma unroll
+          for (int j = 0; j < 2; ++j)
+            if (2 * t + j < p.M) {
+              const uint64_t* q = sl + (size_t)(2 * t + j) * p.N + n;
+              float a0, a1, a2, a3;
+              got &= ll_load(q + 0, e, deadline, &a0);
+              got &= ll_load(q + 1, e, deadline, &a1);
+              got &= ll_load(q + 2, e, deadline, &a2);
+              got &= ll_load(q + 3, e, deadline, &a3);
+              v[j].x += a0;
+              v[j].y += a1;
+              v[j].z += a2;
+              v[j].w += a3;
+            }
+        }
+        if (!got) atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
+        store_y(p, tile, colw, t, v);
+        continue;
+      }
       named_bar_sync(1, kWarps * 32);
       if (threadIdx.x == 0) *s_flag = ar_wait(ar, tile, e) ? 1 : 0;
       named_bar_sync(1, kWarps * 32);
       __threadfence();
-      const int n = tile * kTileN + colw;
       if (n >= p.N) continue;
       float4 v[2];
       v[0] = v[1] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -937,6 +982,7 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
     if (cost > 0.0 && (path == 2 || cost <= sk_cost)) {
       a.cl_size = cs;
       a.cl_count = nc;
+      a.ll = 0;  // the cluster kernel's fused epilogue uses flags
       return launch_kernel_clusters(w4c_kernel<GP, FUSED>, nc * cs, cs, kThreads, CfgC<GP>::kSmem,
                                     stream, early, m_qw, m_sc, m_qz, m_x, a, view);
     }
@@ -990,6 +1036,8 @@ W4Args make_args(const void* a, void* y, int M, int K, int N, int G, void* ws) {
   r.status = reinterpret_cast<int*>(wsb);
   r.counters = reinterpret_cast<int*>(wsb + ws_counters_offset());
   r.partials = reinterpret_cast<float*>(wsb + ws_partials_offset());
+  r.cl_size = r.cl_count = 0;
+  r.ll = 0;
   return r;
 }
 
@@ -1094,8 +1142,10 @@ int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* q
   // Early launch is safe here too: the generation is read after griddepcontrol.wait, and a
   // dependent grid starts only once every CTA of this one is resident, so none of the CTAs that
   // wait for peers in the second phase can be held back.
-  return dispatch<true>(make_args(a, y, M, K, N, G, ws), qw, qz, sc, &v, stream, kWsMaxCtas,
-                        /*early=*/true);
+  W4Args args = make_args(a, y, M, K, N, G, ws);
+  // the low-latency exchange needs 8 bytes per output element in each slot
+  args.ll = v.slot_bytes >= (unsigned long long)M * N * 8 ? 1 : 0;
+  return dispatch<true>(args, qw, qz, sc, &v, stream, kWsMaxCtas, /*early=*/true);
 }
 
 }  // namespace b2

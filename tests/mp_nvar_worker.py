@@ -93,7 +93,7 @@ def main():
 
     ops = entry.load_package().ops()
     M, N, G, K = 8, 5120, 128, 17408
-    ar = vllm_shim.NvlinkAllReduce(cpu, r, list(range(P)), slot_bytes=M * 8192 * 4)
+    ar = vllm_shim.NvlinkAllReduce(cpu, r, list(range(P)), slot_bytes=M * 8192 * 8)
     if not ar.should_use(torch.empty(8 * 5120, dtype=torch.float16, device="cuda")):
         fail("should_use rejects an 80 KB fp16 tensor")
 
