@@ -764,8 +764,13 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
           // (tile * 128 + c0) * M, element idx in the order the threads produce them, so a
           // warp's pushes over NVLink are coalesced (needs N % 128 == 0, checked on the host)
           const size_t at = ((size_t)tile * kTileN + c0) * p.M + idx;
-          for (int r = 0; r < ar.world; ++r)
-            reinterpret_cast<float*>(ar_slot(ar, r, e & 1u, ar.rank))[at] = s;
+          if (p.ll) {
+            for (int r = 0; r < ar.world; ++r)
+              ll_store(reinterpret_cast<uint64_t*>(ar_slot(ar, r, e & 1u, ar.rank)) + at, s, e);
+          } else {
+            for (int r = 0; r < ar.world; ++r)
+              reinterpret_cast<float*>(ar_slot(ar, r, e & 1u, ar.rank))[at] = s;
+          }
         }
       }
     }
@@ -774,19 +779,39 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
     // Every CTA of the cluster has pushed its slice once CTA 0's buffer release completes: CTA 0
     // publishes the tile with one system-scope fence (the peers' pushes happen before it through
     // their CTA barrier and cluster-scope release, which the fence's cumulativity covers).
-    if (FUSED && crank == 0 && tid == 0) {
+    if (FUSED && !p.ll && crank == 0 && tid == 0) {
       if (mbar_wait_cluster(red_empty, (uint32_t)(it & 1), s_abort)) ar_publish(ar, tile, e);
     }
   }
   if constexpr (FUSED) {
     // -------------------------------------------------------------- fused all-reduce, phase 2
+    const unsigned long long deadline = globaltimer_ns() + ar.timeout_ns;
     for (int it = 0; it < ntile; ++it) {
       const int tile = cid + it * NC;
+      const size_t blk = ((size_t)tile * kTileN + c0) * p.M;
+      if (p.ll) {
+        bool got = true;
+        for (int idx = tid; idx < p.M * W; idx += kWarps * 32) {
+          const int m = idx / W, col = c0 + (idx - m * W);
+          const int n = tile * kTileN + col;
+          if (n >= p.N) continue;
+          float s = 0.f;
+          for (int src = 0; src < ar.world; ++src) {
+            float a;
+            got &= ll_load(reinterpret_cast<const uint64_t*>(ar_slot(ar, ar.rank, e & 1u, src)) +
+                               blk + idx,
+                           e, deadline, &a);
+            s += a;
+          }
+          p.y[(size_t)m * p.N + n] = __float2half_rn(s);
+        }
+        if (!got) atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
+        continue;
+      }
       named_bar_sync(1, kWarps * 32);
       if (tid == 0) *s_flag = ar_wait(ar, tile, e) ? 1 : 0;
       named_bar_sync(1, kWarps * 32);
       __threadfence();
-      const size_t blk = ((size_t)tile * kTileN + c0) * p.M;
       for (int idx = tid; idx < p.M * W; idx += kWarps * 32) {
         const int m = idx / W, col = c0 + (idx - m * W);
         const int n = tile * kTileN + col;
@@ -955,12 +980,15 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
 
   // Split-K path. The scratch-only entry point (max_ctas below the workspace bound) always takes
   // stream-K, whose fix-up is what its scratch is for.
-  // Fused launches default to stream-K (measured faster at TP=2: 24.9 us against 38.9 us for the
-  // cluster kernel's fused epilogue); B2_TUNE_W4_PATH = 2 selects the cluster kernel, which needs N
-  // to be a whole number of tiles (its exchange blocks then fit the M x N slot exactly).
+  // Fused launches take the cluster kernel when its exchange blocks fit the slot (N a whole
+  // number of tiles) and the slot holds the 64-bit value+generation words (TP=2 down_proj shard:
+  // 17.5 us, against 20.3 us for stream-K fused and 23.8 us for GEMM + NCCL). With fp32 slots
+  // and flags stream-K fused was faster (24.8 against 29.9 us), so it is the choice there.
   const int path = tuning(B2_TUNE_W4_PATH);
   const bool cluster_ok = !FUSED || N % kTileN == 0;
-  if (cluster_ok && (path == 2 || (path == 0 && !FUSED && max_ctas >= kWsMaxCtas))) {
+  const bool cluster_default = !FUSED || a.ll;
+  if (cluster_ok &&
+      (path == 2 || (path == 0 && cluster_default && max_ctas >= kWsMaxCtas))) {
     const ClusterCaps* cc = nullptr;
     rc = cluster_caps<GP, FUSED>(dev, &cc);
     if (rc) return rc;
@@ -982,7 +1010,6 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
     if (cost > 0.0 && (path == 2 || cost <= sk_cost)) {
       a.cl_size = cs;
       a.cl_count = nc;
-      a.ll = 0;  // the cluster kernel's fused epilogue uses flags
       return launch_kernel_clusters(w4c_kernel<GP, FUSED>, nc * cs, cs, kThreads, CfgC<GP>::kSmem,
                                     stream, early, m_qw, m_sc, m_qz, m_x, a, view);
     }

@@ -198,28 +198,29 @@ def main():
     if ar.status() != 0:
         fail(f"fused status {ar.status()}")
 
-    # 3b. the same layer through the cluster split-K kernel's fused epilogue (B2_TUNE_W4_PATH = 2)
+    # 3b. the same layer through the other split-K kernel's fused epilogue (the default is the
+    # cluster kernel; B2_TUNE_W4_PATH = 1 selects stream-K with its global fix-up)
     from mi50_vllm_lab_b200 import capi
 
     lib = capi.lib()
-    lib.b2_set_tuning(4, 2)
+    lib.b2_set_tuning(4, 1)
     yc = ar.w4_gemm_all_reduce(xs, qws, qzs, scs)
     torch.cuda.synchronize()
     if not gather_equal(yc):
-        fail("cluster fused GEMM+all-reduce results differ across ranks")
+        fail("stream-K fused GEMM+all-reduce results differ across ranks")
     if r == 0:
         st = so.error_stats(yc[:, torch.from_numpy(cols).cuda()].double().cpu().numpy(),
                             gpu_util.w4_ref_sampled(x, qw, qz, sc, cols))
         if not so.within_tolerance(st):
-            fail(f"cluster fused GEMM+all-reduce outside tolerance: {st}")
+            fail(f"stream-K fused GEMM+all-reduce outside tolerance: {st}")
     for _ in range(2):
         yc2 = ar.w4_gemm_all_reduce(xs, qws, qzs, scs)
     if not torch.equal(yc2, yc):
-        fail("cluster fused GEMM+all-reduce not deterministic")
-    t_fused_cluster = graph_time_us(lambda: ar.w4_gemm_all_reduce(xs, qws, qzs, scs))
+        fail("stream-K fused GEMM+all-reduce not deterministic")
+    t_fused_streamk = graph_time_us(lambda: ar.w4_gemm_all_reduce(xs, qws, qzs, scs))
     lib.b2_set_tuning(4, 0)
     if ar.status() != 0:
-        fail(f"cluster fused status {ar.status()}")
+        fail(f"stream-K fused status {ar.status()}")
 
     # 4. timings (max over ranks): fused vs GEMM + NCCL, and the bare all-reduce vs NCCL at 80 KB
     a80 = torch.randn(8 * 5120, device="cuda", dtype=torch.float16, generator=g)
@@ -255,7 +256,7 @@ def main():
         bytes_rank = ks * N // 2 + (ks // G) * N * 2 + (ks // G) * N // 2 + 2 * M * ks + 2 * M * N
         print(json.dumps({"world": P, "config": f"3: down_proj K={K} sharded {P} ways, M={M}, N={N}",
                           "fused_us": round(t_fused, 2),
-                          "fused_cluster_us": round(t_fused_cluster, 2),
+                          "fused_streamk_us": round(t_fused_streamk, 2),
                           "gemm_plus_nccl_us": round(t_unfused, 2),
                           "gemm_only_us": round(t_gemm, 2), "nvlink_ar_80KB_us": round(t_ar, 2),
                           "nccl_ar_80KB_us": round(t_nccl, 2),
