@@ -158,9 +158,11 @@ int b2_registry_unlink(const char* name);
  * NVLink one-shot all-reduce (replaces the host-memory all-reduce of kernels/hostar.cu)
  *
  * Each rank owns a device buffer: a generation counter, per-rank flags and two
- * parity-alternating sets of `world` data slots. A call pushes this rank's data into its slot
- * on every peer over NVLink, publishes a flag with release semantics, waits (bounded) for all
- * peers' flags and sums the `world` slots in rank order 0..world-1 in fp32. Every rank
+ * parity-alternating sets of `world` data slots (allocated at 4x `slot_bytes`). A call pushes
+ * this rank's data into its slot on every peer over NVLink, publishes a flag with release
+ * semantics, waits (bounded) for all peers' flags and sums the `world` slots in rank order
+ * 0..world-1 in fp32. The fused GEMM (b2_w4_gemm_allreduce) instead sends 64-bit
+ * (generation, fp32 value) words that need no flag and no fence. Every rank
  * therefore computes bit-identical results. The generation lives on the device, so calls can
  * be replayed from a CUDA graph (same protocol as kernels/hostar.cu:9-14, generalised to
  * `world` ranks). No TMA, no multicast.

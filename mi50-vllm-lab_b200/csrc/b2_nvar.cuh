@@ -11,6 +11,9 @@
 // e + 2, which a rank reaches only after every peer has published e + 1, which each peer does only
 // after finishing launch e (stream order) - so no slot is overwritten while it is read
 // (the argument of kernels/hostar.cu:9-14, for `world` ranks).
+// When the slot has room (it is allocated at 4x the largest payload), the data instead travel as
+// 64-bit (generation, fp32 value) words that need no flag and no fence (ll_store / ll_gather); the
+// same reuse argument holds with "published e + 1" read as "wrote its words of e + 1".
 #pragma once
 
 #include "b2_device.cuh"
@@ -90,23 +93,39 @@ __device__ __forceinline__ void ll_store(uint64_t* p, float v, uint32_t e) {
   const uint64_t w = ((uint64_t)e << 32) | (uint64_t)__float_as_uint(v);
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-// Wait (bounded by the absolute globaltimer deadline) for generation e's value at p.
-__device__ __forceinline__ bool ll_load(const uint64_t* p, uint32_t e,
-                                        unsigned long long deadline_ns, float* out) {
-  for (unsigned int it = 0; it < kMaxSpin; ++it) {
-    uint64_t w;
-    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-    if ((uint32_t)(w >> 32) == e) {
-      *out = __uint_as_float((uint32_t)w);
-      return true;
-    }
-    if ((it & 15u) == 15u) {
-      if (globaltimer_ns() > deadline_ns) break;
+__device__ __forceinline__ uint64_t ll_peek(const uint64_t* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+// Generation e's values at p[0..n) (n <= N): all n loads are issued before any is checked, so the
+// words that have already landed cost one round trip together; only the missing ones are polled
+// again (bounded by the absolute deadline). Returns false if a word never arrived (its value
+// reads as 0).
+template <int N>
+__device__ __forceinline__ bool ll_gather(const uint64_t* const (&p)[N], int n, uint32_t e,
+                                          unsigned long long deadline_ns, float (&out)[N]) {
+  uint64_t w[N];
+#pragma unroll
+  for (int k = 0; k < N; ++k)
+    if (k < n) w[k] = ll_peek(p[k]);
+  bool ok = true;
+#pragma unroll
+  for (int k = 0; k < N; ++k) {
+    if (k >= n) continue;
+    unsigned int it = 0;
+    while ((uint32_t)(w[k] >> 32) != e) {
+      if (++it >= kMaxSpin || ((it & 15u) == 0 && globaltimer_ns() > deadline_ns)) {
+        ok = false;
+        w[k] = 0;
+        break;
+      }
       __nanosleep(32);
+      w[k] = ll_peek(p[k]);
     }
+    out[k] = __uint_as_float((uint32_t)w[k]);
   }
-  *out = 0.f;
-  return false;
+  return ok;
 }
 
 // Count this CTA as finished; the last CTA of the launch advances the generation. One thread,

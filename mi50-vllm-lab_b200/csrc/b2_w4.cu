@@ -448,15 +448,13 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
           for (int j = 0; j < 2; ++j)
             if (2 * t + j < p.M) {
               const uint64_t* q = sl + (size_t)(2 * t + j) * p.N + n;
-              float a0, a1, a2, a3;
-              got &= ll_load(q + 0, e, deadline, &a0);
-              got &= ll_load(q + 1, e, deadline, &a1);
-              got &= ll_load(q + 2, e, deadline, &a2);
-              got &= ll_load(q + 3, e, deadline, &a3);
-              v[j].x += a0;
-              v[j].y += a1;
-              v[j].z += a2;
-              v[j].w += a3;
+              const uint64_t* ptr[4] = {q, q + 1, q + 2, q + 3};
+              float a[4];
+              got &= ll_gather<4>(ptr, 4, e, deadline, a);
+              v[j].x += a[0];
+              v[j].y += a[1];
+              v[j].z += a[2];
+              v[j].w += a[3];
             }
         }
         if (!got) atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
@@ -795,14 +793,17 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
           const int m = idx / W, col = c0 + (idx - m * W);
           const int n = tile * kTileN + col;
           if (n >= p.N) continue;
+          const uint64_t* ptr[kArMaxWorld];
+#pragma unroll
+          for (int src = 0; src < kArMaxWorld; ++src)
+            ptr[src] = reinterpret_cast<const uint64_t*>(
+                           ar_slot(ar, ar.rank, e & 1u, src < ar.world ? src : 0)) + blk + idx;
+          float a[kArMaxWorld];
+          got &= ll_gather<kArMaxWorld>(ptr, ar.world, e, deadline, a);
           float s = 0.f;
-          for (int src = 0; src < ar.world; ++src) {
-            float a;
-            got &= ll_load(reinterpret_cast<const uint64_t*>(ar_slot(ar, ar.rank, e & 1u, src)) +
-                               blk + idx,
-                           e, deadline, &a);
-            s += a;
-          }
+#pragma unroll
+          for (int src = 0; src < kArMaxWorld; ++src)
+            if (src < ar.world) s += a[src];
           p.y[(size_t)m * p.N + n] = __float2half_rn(s);
         }
         if (!got) atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
