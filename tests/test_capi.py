@@ -141,3 +141,21 @@ def test_registry_put_get_unlink(capi):
     # mappings stay valid after unlink (the reference unlinks right after attaching)
     assert lib.b2_registry_get(reg, 1, out) == 0
     assert lib.b2_registry_close(reg) == 0 and lib.b2_registry_close(other) == 0
+
+
+def test_tuning_presets_from_environment(built):
+    """B2_TUNE="key=value,..." presets the tuning keys before first use (no GPU needed)."""
+    import subprocess
+    import sys
+
+    from conftest import ROOT
+
+    code = ("import sys; sys.path.insert(0, %r); import __graft_entry__ as e; e.load_package(); "
+            "from mi50_vllm_lab_b200 import capi; L = capi.lib(); "
+            "print(L.b2_get_tuning(3), L.b2_get_tuning(4), L.b2_get_tuning(5))") % str(ROOT)
+    env = dict(os.environ, B2_TUNE="4=1,5=7")
+    out = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.split()[-3:] == ["0", "1", "7"]
+

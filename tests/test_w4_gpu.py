@@ -41,6 +41,32 @@ def test_ragged_shapes(ops, oracle, K, N):
     check(run(ops, dev(x), dev(qw), dev(qz), dev(sc)), oracle.w4_ref(x, qw, qz, sc), f"{K}x{N}")
 
 
+@pytest.mark.parametrize("path,cs", [(1, 0), (2, 0), (2, 1), (2, 3), (2, 8), (2, 16)],
+                         ids=["stream-K", "cluster-auto", "cluster-1", "cluster-3", "cluster-8",
+                              "cluster-16"])
+@pytest.mark.parametrize("M,K,N,G", [(8, 2176, 5120, 128), (3, 5120, 992, 128), (8, 4096, 1056, 32),
+                                     (1, 2048, 4128, 64)])
+def test_split_k_paths(capi, ops, oracle, path, cs, M, K, N, G):
+    """Both split-K kernels (stream-K with a global fix-up; thread-block clusters reducing
+    through distributed shared memory) and several cluster sizes, forced with B2_TUNE_W4_PATH /
+    B2_TUNE_W4_CLUSTER, against the oracle; ragged N (partial last tile) included. A cluster
+    size the shape cannot use (more CTAs than k-units) falls back to stream-K."""
+    lib = capi.lib()
+    saved = (lib.b2_get_tuning(4), lib.b2_get_tuning(5))
+    lib.b2_set_tuning(4, path)
+    lib.b2_set_tuning(5, cs)
+    try:
+        x, qw, qz, sc = oracle.gen_w4(M, K, N, G, seed=M * 7 + K + N + cs)
+        y = run(ops, dev(x), dev(qw), dev(qz), dev(sc))
+        check(y, oracle.w4_ref(x, qw, qz, sc), f"path {path} cs {cs} M={M} K={K} N={N} G={G}")
+        y2 = run(ops, dev(x), dev(qw), dev(qz), dev(sc))
+        assert torch.equal(y, y2), f"not deterministic: {mismatch(y, y2)}"
+        assert ops.workspace_status(False) == 0
+    finally:
+        lib.b2_set_tuning(4, saved[0])
+        lib.b2_set_tuning(5, saved[1])
+
+
 def test_config0(ops, oracle):
     """M=7, K=N=4096, G=128, raw max abs error <= 1e-2 as well."""
     x, qw, qz, sc = oracle.gen_w4(7, 4096, 4096, 128, seed=0)
