@@ -9,6 +9,7 @@ collective); `value` is the aggregate HBM throughput of all ranks, timed as the 
     python bench.py [--gpus N] [--steps K] [--warmup W]
     python bench.py --impl reference      # the reference's CPU path (torch dequant+matmul)
     python bench.py --sweep               # every BASELINE config, one JSON line each (not timed by the driver)
+    python bench.py --norm-epilogue       # row-parallel layer + residual add + RMSNorm, fused vs separate
 
 Metric: HBM TB/s of algorithmic bytes (2*N*K + 2*M*K + 2*M*N for fp16; the W4 formula for W4),
 and us per GEMM.
@@ -612,6 +613,106 @@ def run_decode_step(args):
         dist.destroy_process_group()
 
 
+def run_norm_epilogue(args):
+    """Row-parallel W4 layer + residual add + RMSNorm on one GPU (one-rank all-reduce handle):
+    the fused launch (w4gemm_ar_rmsnorm) against the fused GEMM + all-reduce followed by a
+    separate norm - vLLM's own CUDA kernel (torch.ops._C.fused_add_rms_norm) when vLLM loads, and
+    the torch restatement of its reference code (vllm/ir/ops/layernorm.py:48-58). Per-rank
+    shards of o_proj and down_proj at TP 1..8, M=8; graph replay over weight copies that exceed
+    3x L2, as in --sweep. One JSON line per shape."""
+    import torch
+
+    import __graft_entry__ as entry
+
+    ops = entry.load_package().ops()
+    torch.cuda.set_device(0)
+    M, N, G, eps = 8, CFG4["hidden"], CFG4["G"], 1e-6
+    name = f"/b2_bench_norm_{os.getpid()}"
+    h = ops.nvar_create(name, M * N * 8, 0, 1)
+    ops.hostar_unlink(name)
+    try:
+        import vllm._C  # noqa: F401
+
+        vllm_norm = torch.ops._C.fused_add_rms_norm
+    except Exception as e:  # vLLM's compiled ops are optional here
+        vllm_norm = None
+        print(json.dumps({"note": f"vLLM CUDA ops unavailable: {type(e).__name__}: {e}"[:200]}),
+              flush=True)
+    l2 = torch.cuda.get_device_properties(0).L2_cache_size
+    g = torch.Generator(device="cuda").manual_seed(11)
+    w = (1.0 + (torch.rand(N, device="cuda", generator=g) - 0.5) * 0.4).half()
+    res0 = (torch.randn(M, N, device="cuda", generator=g) * 4).half()
+
+    def torch_norm(x, r):
+        xf = x.float() + r.float()
+        r.copy_(xf.half())
+        var = xf.pow(2).mean(dim=-1, keepdim=True)
+        return (xf * torch.rsqrt(var + eps)).half() * w
+
+    for layer, K_full in (("down", CFG4["inter"]), ("o_proj", CFG4["o_in"])):
+        for P in (1, 2, 4, 8):
+            K = K_full // P
+            copies = max(1, int(3 * l2 // (K * N // 2)) + 1)
+            # small activations: the residual grows by y at every replayed call
+            x = (torch.randn(M, K, device="cuda", generator=g) * 0.01).half()
+            ws = [(torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32,
+                                 generator=g),
+                   torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda",
+                                 dtype=torch.int32, generator=g),
+                   (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half())
+                  for _ in range(copies)]
+            r = res0.clone()
+            variants = {
+                "gemm_ar": lambda t: ops.w4gemm_ar(x, *t, h),
+                "gemm_ar_norm_fused": lambda t: ops.w4gemm_ar_rmsnorm(x, *t, h, r, w, eps),
+                "gemm_ar_then_torch_norm": lambda t: torch_norm(ops.w4gemm_ar(x, *t, h), r),
+            }
+            if vllm_norm is not None:
+                def vl(t):
+                    y = ops.w4gemm_ar(x, *t, h)
+                    vllm_norm(y, r, w, eps)
+                    return y
+                variants["gemm_ar_then_vllm_norm"] = vl
+            row = {"workload": f"{layer} shard TP{P}", "M": M, "K": K, "N": N, "G": G,
+                   "l2_rotation_copies": copies}
+            for vname, fn in variants.items():
+                reps = max(copies, min(64, 20 * copies)) // copies * copies
+                try:
+                    for t in ws:
+                        fn(t)
+                    torch.cuda.synchronize()
+                except RuntimeError as e:  # e.g. a library kernel built for other GPUs
+                    row[vname + "_error"] = str(e)[:160]
+                    continue
+                graph = torch.cuda.CUDAGraph()
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(s):
+                    with torch.cuda.graph(graph, stream=s):
+                        for i in range(reps):
+                            fn(ws[i % copies])
+                torch.cuda.current_stream().wait_stream(s)
+                for _ in range(args.warmup):
+                    graph.replay()
+                torch.cuda.synchronize()
+                st = torch.cuda.current_stream()
+                times = []
+                for _ in range(max(3, args.steps // reps)):
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    graph.replay()
+                    e1.record(st)
+                    e1.synchronize()
+                    times.append(e0.elapsed_time(e1) * 1e3 / reps)
+                row[vname + "_us"] = round(statistics.median(times), 2)
+                del graph
+            row["status"] = int(ops.nvar_status(h, False))
+            print(json.dumps(row), flush=True)
+            del ws
+            torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -624,6 +725,8 @@ def main():
     ap.add_argument("--only", default="", help="with --sweep: workloads whose name contains one of these comma-separated "
                          "strings; with --profile: the first workload whose name contains it")
     ap.add_argument("--profile", action="store_true", help="eager launches of one --only workload (for ncu)")
+    ap.add_argument("--norm-epilogue", action="store_true",
+                    help="row-parallel W4 layer + residual add + RMSNorm: fused vs separate, 1 GPU")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--tune", action="append", default=[], metavar="KEY=VALUE",
@@ -641,6 +744,8 @@ def main():
         run_sweep(args)
     elif args.decode_step:
         run_decode_step(args)
+    elif args.norm_epilogue:
+        run_norm_epilogue(args)
     else:
         run_gpu(args)
 

@@ -8,6 +8,8 @@
  *   - a W4A16 GEMM over GPTQ/Exllama-shuffled 4-bit weights                (b2_w4_gemm)
  *   - a one-shot all-reduce over NVLink peer memory                        (b2_nvar_*)
  *   - the W4A16 GEMM with that all-reduce fused into its epilogue          (b2_w4_gemm_allreduce)
+ *   - the same, followed in the same launch by the residual add + RMSNorm
+ *     of the decoder layer                                        (b2_w4_gemm_allreduce_rmsnorm)
  * Every compute entry point launches on the caller's stream, never synchronises and never
  * allocates, so it can be captured in a CUDA graph.
  *
@@ -190,7 +192,25 @@ int b2_nvar_allreduce(b2_nvar* ar, const void* in, void* out, size_t count, int 
 int b2_w4_gemm_allreduce(b2_nvar* ar, const void* a, const void* qw, const void* qz,
                          const void* sc, void* y, int M, int K, int N, int group_size, void* ws,
                          size_t ws_bytes, void* stream);
-/* Synchronously read the device error word of the handle (0 or B2_ERR_TIMEOUT). */
+/* The same layer followed, in the same launch, by the residual add + RMSNorm that the decoder
+ * layer runs on the all-reduced output (vLLM's fused_add_rms_norm, vllm/ir/ops/layernorm.py:40-60
+ * in vLLM 0.22; no counterpart in the reference's library):
+ *   s        = allreduce_over_ranks(a_rank @ dequant(qw_rank, ...))     as b2_w4_gemm_allreduce
+ *   x        = float(fp16(s)) + float(residual)                         fp32
+ *   residual <- fp16(x)                                                 in place
+ *   y        = fp16(fp16(x * rsqrt(sum_n(x^2) / N + eps)) * norm_weight[n])
+ * residual : [M, N] fp16, read and written; norm_weight : [N] fp16; both 8-byte aligned, and
+ * y, residual and norm_weight must not overlap. 0 <= eps <= 1. The row sums are added in a fixed
+ * order, so y and residual are bit-identical on every rank and from call to call. One
+ * grid-wide barrier inside the kernel (bounded by the handle's timeout; B2_ERR_TIMEOUT in the
+ * handle's status if it gives up). */
+int b2_w4_gemm_allreduce_rmsnorm(b2_nvar* ar, const void* a, const void* qw, const void* qz,
+                                 const void* sc, void* residual, const void* norm_weight,
+                                 float eps, void* y, int M, int K, int N, int group_size,
+                                 void* ws, size_t ws_bytes, void* stream);
+/* Synchronously read the device error word of the handle (0 or B2_ERR_TIMEOUT). Clearing a
+ * timeout also resets the grid-wide barrier count of b2_w4_gemm_allreduce_rmsnorm, which a
+ * launch that gave up may have left behind: clear it before the next call. */
 int b2_nvar_status(b2_nvar* ar, int clear, int* device_status);
 int b2_nvar_rank(const b2_nvar* ar);
 int b2_nvar_world(const b2_nvar* ar);

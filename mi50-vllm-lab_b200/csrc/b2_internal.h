@@ -36,12 +36,14 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uin
               uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
               CUtensorMapSwizzle swizzle);
 
-// Workspace layout: [status words][tile counters][partial slots].
+// Workspace layout: [status words][tile counters][partial slots][row sums of the fused RMSNorm,
+// kMaxM floats per CTA].
 constexpr size_t kWsStatusBytes = 256;
 constexpr int kWsMaxTiles = 65536;
 constexpr int kWsMaxCtas = 1024;
 size_t ws_counters_offset();
 size_t ws_partials_offset();
+size_t ws_norm_offset();
 size_t ws_total_bytes();
 
 // Tuning knobs (b2_set_tuning).

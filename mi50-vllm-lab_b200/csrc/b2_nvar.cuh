@@ -30,6 +30,10 @@ struct ArHeader {
   uint32_t gen;   // completed launches
   uint32_t done;  // CTAs of the running launch that finished
   int status;     // 0 or B2_ERR_TIMEOUT
+  // grid-wide barrier of a fused launch that normalises rows (residual add + RMSNorm): CTAs
+  // arrived so far, and the generation of the last launch whose CTAs all arrived
+  uint32_t norm_count;
+  uint32_t norm_gen;
 };
 
 // Kernel-parameter view of one all-reduce handle.

@@ -161,9 +161,10 @@ size_t ws_partials_offset() {
   size_t off = kWsStatusBytes + (size_t)kWsMaxTiles * sizeof(int);
   return (off + 255) & ~(size_t)255;
 }
-size_t ws_total_bytes() {
+size_t ws_norm_offset() {
   return ws_partials_offset() + (size_t)kWsMaxCtas * 2 * kSlotFloats * sizeof(float);
 }
+size_t ws_total_bytes() { return ws_norm_offset() + (size_t)kWsMaxCtas * kMaxM * sizeof(float); }
 
 // ----------------------------------------------------------------------------------------------
 // Tuning

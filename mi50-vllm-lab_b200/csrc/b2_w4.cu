@@ -48,6 +48,8 @@ constexpr int kQwBox = 16 * 128;            // 16 word rows x 32 columns x 4 B (
 constexpr int kQwStage = kWarps * kQwBox;   // 8 KB
 
 constexpr int align128(int v) { return (v + 127) & ~127; }
+// shared memory of the RMSNorm epilogue: per-warp row sums [kWarps][kMaxM], then rstd [kMaxM]
+constexpr int kNormFloats = (kWarps + 1) * kMaxM;
 
 // Shared memory of one CTA (offsets from a 1024-byte aligned base). Every TMA destination must
 // start on a 128-byte boundary, and the swizzled qw boxes on a 1024-byte one.
@@ -69,7 +71,8 @@ struct Cfg {
   static constexpr int kScOff = kXOff + kStages * kXBytes;
   static constexpr int kQzOff = kScOff + kStages * kScStride;
   static constexpr int kBarOff = kQzOff + kStages * kQzStride;
-  static constexpr int kSmem = 1024 + kBarOff + 2 * kStages * 8 + 32;
+  static constexpr int kNormOff = align128(kBarOff + 2 * kStages * 8 + 32);  // kNormFloats fp32
+  static constexpr int kSmem = 1024 + kNormOff + kNormFloats * 4;
   static_assert(kQwBox % 1024 == 0 && kQwStage % 1024 == 0, "swizzled boxes need 1024 B");
   static_assert(kXOff % 1024 == 0 && kXBytes % 1024 == 0, "swizzled boxes need 1024 B");
   static_assert(kScOff % 128 == 0 && kScStride % 128 == 0, "TMA destination alignment");
@@ -87,6 +90,12 @@ struct W4Args {
   int* status;
   int cl_size, cl_count;  // cluster kernel: CTAs per cluster, clusters
   int ll;                 // fused stream-K: exchange as 64-bit value+generation words
+  // fused launches only: residual add + RMSNorm of the all-reduced rows (norm != 0)
+  int norm;
+  float eps;
+  const __half* nw;  // [N] norm weight
+  __half* res;       // [M, N] residual: read, then overwritten with the sum
+  float* npart;      // [grid][kMaxM] per-CTA sums of squares (workspace)
 };
 
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t b, uint32_t c) {
@@ -134,6 +143,139 @@ __device__ __forceinline__ void store_y(const W4Args& p, int tile, int colw, int
     u.y = *reinterpret_cast<uint32_t*>(&h1);
     *reinterpret_cast<uint2*>(p.y + (size_t)m * p.N + n) = u;
   }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Residual add + RMSNorm of the all-reduced rows (fused launches with p.norm). Follows vLLM's
+// fused_add_rms_norm (vllm/ir/ops/layernorm.py:40-60 in vLLM 0.22), which the decoder layers of
+// the reference's models run on the all-reduced output of o_proj and down_proj:
+//   x        = float(y) + float(residual)      y: the fp16 all-reduce result; x stays fp32
+//   residual <- fp16(x)
+//   out      = fp16(fp16(x * rsqrt(sum_n(x^2) / N + eps)) * weight)
+// A row's sum needs every CTA's columns. Phase a, while the all-reduced sums are stored: y gets
+// fp16(sum) and each thread adds x^2 per row over its elements in a fixed order. norm_rstd:
+// the CTA's row sums go to the workspace, one grid-wide barrier, then every CTA adds all CTAs'
+// sums in CTA order, so every CTA (and every rank) computes the same rstd bit for bit. Phase c:
+// each thread re-reads y and the still untouched residual of its own elements and writes the
+// new residual and `out` (into y).
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float norm_x(__half yh, __half r) {
+  return __half2float(yh) + __half2float(r);
+}
+__device__ __forceinline__ __half norm_out(float x, float rstd, __half w) {
+  return __float2half_rn(__half2float(__float2half_rn(x * rstd)) * __half2float(w));
+}
+// ss[m] += q for a row index known only at run time (kept in registers)
+__device__ __forceinline__ void row_add(float (&ss)[kMaxM], int m, float q) {
+#pragma unroll
+  for (int i = 0; i < kMaxM; ++i)
+    if (i == m) ss[i] += q;
+}
+
+// Phase a for the lane layout of store_y: columns n..n+3 of rows 2t, 2t+1 with fp32 sums v.
+__device__ __forceinline__ void norm_accum_lane(const W4Args& p, int t, int n,
+                                                const float4 (&v)[2], float (&ss)[kMaxM]) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int m = 2 * t + j;
+    if (m >= p.M) continue;
+    const uint2 rv = *reinterpret_cast<const uint2*>(p.res + (size_t)m * p.N + n);
+    const __half* r = reinterpret_cast<const __half*>(&rv);
+    const float x0 = norm_x(__float2half_rn(v[j].x), r[0]);
+    const float x1 = norm_x(__float2half_rn(v[j].y), r[1]);
+    const float x2 = norm_x(__float2half_rn(v[j].z), r[2]);
+    const float x3 = norm_x(__float2half_rn(v[j].w), r[3]);
+    row_add(ss, m, fmaf(x3, x3, fmaf(x2, x2, fmaf(x1, x1, x0 * x0))));
+  }
+}
+
+// Phase c for columns n..n+3 of row m.
+__device__ __forceinline__ void norm_finish4(const W4Args& p, int m, int n, float rstd) {
+  const size_t o = (size_t)m * p.N + n;
+  uint2 yv = *reinterpret_cast<const uint2*>(p.y + o);
+  uint2 rv = *reinterpret_cast<const uint2*>(p.res + o);
+  const uint2 wv = *reinterpret_cast<const uint2*>(p.nw + n);
+  __half* yh = reinterpret_cast<__half*>(&yv);
+  __half* rh = reinterpret_cast<__half*>(&rv);
+  const __half* wh = reinterpret_cast<const __half*>(&wv);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float x = norm_x(yh[i], rh[i]);
+    rh[i] = __float2half_rn(x);
+    yh[i] = norm_out(x, rstd, wh[i]);
+  }
+  *reinterpret_cast<uint2*>(p.res + o) = rv;
+  *reinterpret_cast<uint2*>(p.y + o) = yv;
+}
+// Phase c for one element.
+__device__ __forceinline__ void norm_finish1(const W4Args& p, int m, int n, float rstd) {
+  const size_t o = (size_t)m * p.N + n;
+  const float x = norm_x(p.y[o], p.res[o]);
+  p.res[o] = __float2half_rn(x);
+  p.y[o] = norm_out(x, rstd, p.nw[n]);
+}
+
+// Called by every consumer thread of every CTA with its per-row sums of squares. Leaves
+// rstd[m] for m < M at s_norm[kWarps * kMaxM + m]. Returns false if the grid-wide barrier gave
+// up (after the handle's timeout; the caller records B2_ERR_TIMEOUT).
+__device__ __forceinline__ bool norm_rstd(const W4Args& p, const ArView& ar, uint32_t e,
+                                          const float (&ss)[kMaxM], float* s_norm,
+                                          volatile int* s_flag) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // the CTA's row sums: a fixed shuffle tree per warp, then the warps in order
+#pragma unroll
+  for (int m = 0; m < kMaxM; ++m) {
+    float v = ss[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) s_norm[warp * kMaxM + m] = v;
+  }
+  named_bar_sync(1, kWarps * 32);
+  if (tid < kMaxM) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) v += s_norm[w * kMaxM + tid];
+    p.npart[(size_t)blockIdx.x * kMaxM + tid] = v;
+  }
+  named_bar_sync(1, kWarps * 32);
+  // grid-wide barrier: the last CTA to arrive resets the count and releases generation e. The
+  // fence before each arrival makes the CTA's row sums (ordered before it by the CTA barrier)
+  // visible to whoever observes the arrival.
+  if (tid == 0) {
+    ArHeader* h = ar_header(ar);
+    bool ok = true;
+    __threadfence();
+    if (atomicAdd(&h->norm_count, 1u) == gridDim.x - 1) {
+      atomicExch(&h->norm_count, 0u);
+      __threadfence();
+      st_release_sys(&h->norm_gen, e);
+    } else {
+      const unsigned long long t0 = globaltimer_ns();
+      unsigned int it = 0;
+      while ((int)(ld_acquire_sys(&h->norm_gen) - e) < 0) {
+        if (++it >= kMaxSpin || ((it & 15u) == 0 && globaltimer_ns() - t0 > ar.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    *s_flag = ok ? 1 : 0;
+  }
+  named_bar_sync(1, kWarps * 32);
+  __threadfence();
+  const bool ok = *s_flag != 0;
+  // rstd of row m (warp m % 4): lane l adds the sums of CTAs l, l + 32, ... in order, then a
+  // fixed shuffle tree
+  for (int m = warp; m < p.M; m += kWarps) {
+    float v = 0.f;
+    for (int b = lane; b < (int)gridDim.x; b += 32) v += __ldcg(p.npart + (size_t)b * kMaxM + m);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) s_norm[kWarps * kMaxM + m] = rsqrtf(v / (float)p.N + p.eps);
+  }
+  named_bar_sync(1, kWarps * 32);
+  return ok;
 }
 
 // A = (q - z) in fp16 (exact, see dequant_word) against B = x; the fp32 sum of each quantization
@@ -435,6 +577,9 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
     // -------------------------------------------------------------- fused all-reduce, phase 2
     // CTA b adds tiles b, b + grid, ... over all ranks in rank order and writes the fp16 result.
     const unsigned long long deadline = globaltimer_ns() + ar.timeout_ns;
+    float ss[kMaxM];  // RMSNorm: this thread's sums of squares per row
+#pragma unroll
+    for (int i = 0; i < kMaxM; ++i) ss[i] = 0.f;
     for (int tile = blockIdx.x; tile < sk.tiles; tile += gridDim.x) {
       const int n = tile * kTileN + colw;
       if (p.ll) {
@@ -459,6 +604,7 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
         }
         if (!got) atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
         store_y(p, tile, colw, t, v);
+        if (p.norm) norm_accum_lane(p, t, n, v, ss);
         continue;
       }
       named_bar_sync(1, kWarps * 32);
@@ -482,6 +628,19 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
           }
       }
       store_y(p, tile, colw, t, v);
+      if (p.norm) norm_accum_lane(p, t, n, v, ss);
+    }
+    if (p.norm) {
+      float* s_norm = reinterpret_cast<float*>(smem + C::kNormOff);
+      if (!norm_rstd(p, ar, e, ss, s_norm, s_flag) && threadIdx.x == 0)
+        atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
+      for (int tile = blockIdx.x; tile < sk.tiles; tile += gridDim.x) {
+        const int n = tile * kTileN + colw;
+        if (n >= p.N) continue;
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          if (2 * t + j < p.M) norm_finish4(p, 2 * t + j, n, s_norm[kWarps * kMaxM + 2 * t + j]);
+      }
     }
     named_bar_sync(1, kWarps * 32);
     if (threadIdx.x == 0) ar_finish(ar, e);
@@ -511,7 +670,8 @@ struct CfgC {
   static constexpr int kQzOff = kScOff + kStages * kScStride;
   static constexpr int kRedOff = kQzOff + kStages * kQzStride;  // [8 rows][128 columns] fp32
   static constexpr int kBarOff = kRedOff + kMaxM * kTileN * 4;
-  static constexpr int kSmem = 1024 + kBarOff + (2 * kStages + 2) * 8 + 32;
+  static constexpr int kNormOff = align128(kBarOff + (2 * kStages + 2) * 8 + 32);
+  static constexpr int kSmem = 1024 + kNormOff + kNormFloats * 4;
   static_assert(kXOff % 1024 == 0 && kXBytes % 1024 == 0, "swizzled boxes need 1024 B");
   static_assert(kScOff % 128 == 0 && kQzOff % 128 == 0 && kRedOff % 128 == 0, "alignment");
 };
@@ -784,6 +944,9 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
   if constexpr (FUSED) {
     // -------------------------------------------------------------- fused all-reduce, phase 2
     const unsigned long long deadline = globaltimer_ns() + ar.timeout_ns;
+    float ss[kMaxM];  // RMSNorm: this thread's sums of squares per row
+#pragma unroll
+    for (int i = 0; i < kMaxM; ++i) ss[i] = 0.f;
     for (int it = 0; it < ntile; ++it) {
       const int tile = cid + it * NC;
       const size_t blk = ((size_t)tile * kTileN + c0) * p.M;
@@ -804,7 +967,12 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
 #pragma unroll
           for (int src = 0; src < kArMaxWorld; ++src)
             if (src < ar.world) s += a[src];
-          p.y[(size_t)m * p.N + n] = __float2half_rn(s);
+          const __half yh = __float2half_rn(s);
+          p.y[(size_t)m * p.N + n] = yh;
+          if (p.norm) {
+            const float x = norm_x(yh, p.res[(size_t)m * p.N + n]);
+            row_add(ss, m, x * x);
+          }
         }
         if (!got) atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
         continue;
@@ -820,7 +988,24 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
         float s = 0.f;
         for (int src = 0; src < ar.world; ++src)
           s += __ldcg(reinterpret_cast<const float*>(ar_slot(ar, ar.rank, e & 1u, src)) + blk + idx);
-        p.y[(size_t)m * p.N + n] = __float2half_rn(s);
+        const __half yh = __float2half_rn(s);
+        p.y[(size_t)m * p.N + n] = yh;
+        if (p.norm) {
+          const float x = norm_x(yh, p.res[(size_t)m * p.N + n]);
+          row_add(ss, m, x * x);
+        }
+      }
+    }
+    if (p.norm) {
+      float* s_norm = reinterpret_cast<float*>(smem + C::kNormOff);
+      if (!norm_rstd(p, ar, e, ss, s_norm, s_flag) && tid == 0)
+        atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
+      for (int it = 0; it < ntile; ++it) {
+        const int tile = cid + it * NC;
+        for (int idx = tid; idx < p.M * W; idx += kWarps * 32) {
+          const int m = idx / W, n = tile * kTileN + c0 + (idx - m * W);
+          if (n < p.N) norm_finish1(p, m, n, s_norm[kWarps * kMaxM + m]);
+        }
       }
     }
     named_bar_sync(1, kWarps * 32);
@@ -1008,7 +1193,8 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
       for (int i = 1; i <= 16; ++i) std::fprintf(stderr, " %d", cc->max_clusters[i]);
       std::fprintf(stderr, "\n");
     }
-    if (cost > 0.0 && (path == 2 || cost <= sk_cost)) {
+    // (the RMSNorm epilogue keeps kMaxM row sums per CTA in the workspace: kWsMaxCtas CTAs)
+    if (cost > 0.0 && (path == 2 || cost <= sk_cost) && (!a.norm || nc * cs <= kWsMaxCtas)) {
       a.cl_size = cs;
       a.cl_count = nc;
       return launch_kernel_clusters(w4c_kernel<GP, FUSED>, nc * cs, cs, kThreads, CfgC<GP>::kSmem,
@@ -1066,6 +1252,11 @@ W4Args make_args(const void* a, void* y, int M, int K, int N, int G, void* ws) {
   r.partials = reinterpret_cast<float*>(wsb + ws_partials_offset());
   r.cl_size = r.cl_count = 0;
   r.ll = 0;
+  r.norm = 0;
+  r.eps = 0.f;
+  r.nw = nullptr;
+  r.res = nullptr;
+  r.npart = nullptr;
   return r;
 }
 
@@ -1156,11 +1347,30 @@ int launch_w4_noalloc(const void* a, const void* qw, const void* qz, const void*
   return dispatch<false>(args, qw, qz, sc, nullptr, stream, kNoAllocMaxCtas);
 }
 
+// `residual` and `nw` non-null: the residual add + RMSNorm epilogue (see norm_rstd).
 int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* qz, const void* sc,
                         void* y, int M, int K, int N, int G, void* ws, size_t ws_bytes,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, void* residual = nullptr, const void* nw = nullptr,
+                        float eps = 0.f) {
   int rc = validate(a, qw, qz, sc, y, M, K, N, G, ws, ws_bytes);
   if (rc) return rc;
+  const bool norm = residual || nw;
+  if (norm) {
+    if (!residual || !nw) return fail(B2_ERR_INVALID_ARG, "w4_allreduce_rmsnorm: null pointer");
+    if ((reinterpret_cast<uintptr_t>(residual) & 7u) != 0 ||
+        (reinterpret_cast<uintptr_t>(nw) & 7u) != 0)
+      return fail(B2_ERR_INVALID_ARG,
+                  "w4_allreduce_rmsnorm: residual and norm_weight must be 8-byte aligned");
+    const uintptr_t yb = reinterpret_cast<uintptr_t>(y), rb = reinterpret_cast<uintptr_t>(residual);
+    const uintptr_t wb = reinterpret_cast<uintptr_t>(nw);
+    const uintptr_t mn = (uintptr_t)M * N * 2, nb = (uintptr_t)N * 2;
+    if ((yb < rb + mn && rb < yb + mn) || (yb < wb + nb && wb < yb + mn) ||
+        (rb < wb + nb && wb < rb + mn))
+      return fail(B2_ERR_INVALID_ARG,
+                  "w4_allreduce_rmsnorm: y, residual and norm_weight must not overlap");
+    if (!(eps >= 0.f) || eps > 1.f)
+      return fail(B2_ERR_INVALID_ARG, "w4_allreduce_rmsnorm: eps %g outside [0, 1]", (double)eps);
+  }
   ArView v;
   int tiles_cap = 0;
   rc = nvar_view(h, &v, (size_t)M * N * sizeof(float), &tiles_cap);
@@ -1173,6 +1383,13 @@ int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* q
   W4Args args = make_args(a, y, M, K, N, G, ws);
   // the low-latency exchange needs 8 bytes per output element in each slot
   args.ll = v.slot_bytes >= (unsigned long long)M * N * 8 ? 1 : 0;
+  if (norm) {
+    args.norm = 1;
+    args.eps = eps;
+    args.res = static_cast<__half*>(residual);
+    args.nw = static_cast<const __half*>(nw);
+    args.npart = reinterpret_cast<float*>(static_cast<char*>(ws) + ws_norm_offset());
+  }
   return dispatch<true>(args, qw, qz, sc, &v, stream, kWsMaxCtas, /*early=*/true);
 }
 
@@ -1191,6 +1408,18 @@ extern "C" int b2_w4_gemm_allreduce(b2_nvar* ar, const void* a, const void* qw, 
   if (!ar) return b2::fail(B2_ERR_STATE, "w4_allreduce: null all-reduce handle");
   return b2::launch_w4_allreduce(ar, a, qw, qz, sc, y, M, K, N, group_size, ws, ws_bytes,
                                  static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b2_w4_gemm_allreduce_rmsnorm(b2_nvar* ar, const void* a, const void* qw,
+                                            const void* qz, const void* sc, void* residual,
+                                            const void* norm_weight, float eps, void* y, int M,
+                                            int K, int N, int group_size, void* ws,
+                                            size_t ws_bytes, void* stream) {
+  if (!ar) return b2::fail(B2_ERR_STATE, "w4_allreduce_rmsnorm: null all-reduce handle");
+  if (!residual || !norm_weight)
+    return b2::fail(B2_ERR_INVALID_ARG, "w4_allreduce_rmsnorm: null residual or norm_weight");
+  return b2::launch_w4_allreduce(ar, a, qw, qz, sc, y, M, K, N, group_size, ws, ws_bytes,
+                                 static_cast<cudaStream_t>(stream), residual, norm_weight, eps);
 }
 
 // The W4A16 GEMM without a caller-supplied workspace; see include/b2_skinny.h.

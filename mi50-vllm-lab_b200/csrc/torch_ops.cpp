@@ -6,7 +6,8 @@
 //   w4gemm(Tensor a, Tensor qw, Tensor qz, Tensor sc, int kw, int waves) kernels/w4.cu:506-509
 //   hostar_create / hostar_unlink / hostar_max_bytes / hostar_allreduce kernels/hostar.cu:155-166
 // plus operators the reference does not have (N-rank NVLink all-reduce, the W4 GEMM with the
-// all-reduce fused into its epilogue, status and tuning). Device operators are registered on the
+// all-reduce fused into its epilogue, optionally followed by the residual add + RMSNorm, status
+// and tuning). Device operators are registered on the
 // CUDA dispatch key and launch on the current stream; host operators on
 // CompositeExplicitAutograd, as in the reference. Errors become RuntimeError via TORCH_CHECK.
 //
@@ -255,6 +256,36 @@ at::Tensor w4gemm_ar(const at::Tensor& a, const at::Tensor& qw, const at::Tensor
   return y;
 }
 
+// w4gemm_ar followed, in the same launch, by vLLM's fused residual add + RMSNorm
+// (b2_w4_gemm_allreduce_rmsnorm): `residual` becomes residual + all-reduced rows, in place, and
+// the normalised rows are returned.
+at::Tensor w4gemm_ar_rmsnorm(const at::Tensor& a, const at::Tensor& qw, const at::Tensor& qz,
+                             const at::Tensor& sc, int64_t handle, at::Tensor& residual,
+                             const at::Tensor& weight, double eps) {
+  const char* op = "w4gemm_ar_rmsnorm";
+  const int G = check_w4(a, qw, qz, sc, op);
+  check_cuda_half(residual, op, "residual");
+  check_cuda_half(weight, op, "weight");
+  const int64_t M = a.size(0), K = a.size(1), N = qw.size(1);
+  TORCH_CHECK(residual.dim() == 2 && residual.size(0) == M && residual.size(1) == N, op,
+              ": residual must be [M, N]; got ", residual.sizes());
+  TORCH_CHECK(weight.dim() == 1 && weight.size(0) == N, op, ": weight must be [N]; got ",
+              weight.sizes());
+  TORCH_CHECK(residual.device() == a.device() && weight.device() == a.device(), op,
+              ": residual and weight must be on the input's device");
+  ArEntry& e = connected_entry(handle, op);
+  c10::cuda::CUDAGuard guard(a.device());
+  auto y = at::empty({M, N}, a.options());
+  const int dev = a.get_device();
+  void* ws = workspace(dev);
+  const int rc = b2_w4_gemm_allreduce_rmsnorm(
+      e.ar, a.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(), residual.data_ptr(),
+      weight.data_ptr(), (float)eps, y.data_ptr(), (int)M, (int)K, (int)N, G, ws,
+      b2_workspace_bytes(dev), c10::cuda::getCurrentCUDAStream(dev).stream());
+  TORCH_CHECK(rc == B2_OK, "gfx906_skinny.w4gemm_ar_rmsnorm: ", detail(rc));
+  return y;
+}
+
 int64_t nvar_status(int64_t handle, bool clear) {
   ArEntry* e;
   {
@@ -306,6 +337,8 @@ TORCH_LIBRARY(gfx906_skinny, m) {
   m.def("nvar_connect(int handle) -> ()");
   m.def("nvar_allreduce(Tensor inp, int handle) -> Tensor");
   m.def("w4gemm_ar(Tensor a, Tensor qw, Tensor qz, Tensor sc, int handle) -> Tensor");
+  m.def("w4gemm_ar_rmsnorm(Tensor a, Tensor qw, Tensor qz, Tensor sc, int handle, "
+        "Tensor(a!) residual, Tensor weight, float eps) -> Tensor");
   m.def("nvar_status(int handle, bool clear=False) -> int");
   m.def("nvar_set_timeout_ms(int handle, int ms) -> ()");
   m.def("workspace_status(bool clear=False) -> int");
@@ -318,6 +351,7 @@ TORCH_LIBRARY_IMPL(gfx906_skinny, CUDA, m) {
   m.impl("hostar_allreduce", &hostar_allreduce);
   m.impl("nvar_allreduce", &nvar_allreduce);
   m.impl("w4gemm_ar", &w4gemm_ar);
+  m.impl("w4gemm_ar_rmsnorm", &w4gemm_ar_rmsnorm);
 }
 
 TORCH_LIBRARY_IMPL(gfx906_skinny, Meta, m) {

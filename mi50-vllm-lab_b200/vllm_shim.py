@@ -129,6 +129,13 @@ class NvlinkAllReduce:
         """Row-parallel W4 layer: this rank's K-shard GEMM with the all-reduce fused in."""
         return self.ops.w4gemm_ar(x, w_q, w_zp, w_s, self.handle)
 
+    def w4_gemm_all_reduce_rmsnorm(self, x, w_q, w_zp, w_s, residual, weight,
+                                   eps: float) -> torch.Tensor:
+        """The same layer followed, in the same launch, by the decoder layer's residual add +
+        RMSNorm (vLLM's fused_add_rms_norm): ``residual`` is updated in place, the normalised
+        rows are returned."""
+        return self.ops.w4gemm_ar_rmsnorm(x, w_q, w_zp, w_s, self.handle, residual, weight, eps)
+
     def status(self, clear: bool = False) -> int:
         return int(self.ops.nvar_status(self.handle, clear))
 

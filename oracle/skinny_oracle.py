@@ -106,6 +106,37 @@ def allreduce_ref(parts: list[np.ndarray]) -> np.ndarray:
 
 
 # --------------------------------------------------------------------------------------------
+# Residual add + RMSNorm of the all-reduced rows. The reference's models (Qwen3 family, served
+# by its vLLM fork) run vLLM's fused_add_rms_norm on the all-reduced output of every o_proj and
+# down_proj. Third-party algorithm: vLLM 0.22.0, vllm/ir/ops/layernorm.py:40-58 (its reference
+# semantics; vLLM's CUDA kernel must match it within atol 1e-2 / rtol 2e-3, :61-62).
+# --------------------------------------------------------------------------------------------
+
+
+def add_rmsnorm_ref(y: np.ndarray, residual: np.ndarray, weight: np.ndarray, eps: float):
+    """(out, new_residual) for y, residual [M, N] fp16 and weight [N] fp16:
+    x = fp32(y) + fp32(residual) (:49-50); new_residual = fp16(x) (:51);
+    out = fp16(fp16(x * rsqrt(mean(x^2) + eps)) * weight) (:54-58). The mean is taken in float64
+    and rounded once to fp32, rsqrt likewise (torch computes both in fp32; the two differ by at
+    most an fp32 ulp or two, which moves an fp16 output by one ulp at most, and rarely)."""
+    x = y.astype(np.float32) + residual.astype(np.float32)
+    new_res = x.astype(np.float16)
+    var = (x.astype(np.float64) ** 2).mean(axis=-1, keepdims=True).astype(np.float32)
+    rstd = (1.0 / np.sqrt((var + np.float32(eps)).astype(np.float64))).astype(np.float32)
+    h = (x * rstd).astype(np.float16)
+    out = (h.astype(np.float32) * weight.astype(np.float32)).astype(np.float16)
+    return out, new_res
+
+
+def fp16_ulp_distance(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """How many fp16 values lie between a and b (0 when equal; +0 and -0 count as equal)."""
+    def ordered(v):
+        i = np.ascontiguousarray(v, dtype=np.float16).view(np.int16).astype(np.int32)
+        return np.where(i < 0, -(i & 0x7FFF), i)
+    return np.abs(ordered(a) - ordered(b))
+
+
+# --------------------------------------------------------------------------------------------
 # Seeded inputs (the benchmark configurations; numpy PCG64, stable across versions)
 # --------------------------------------------------------------------------------------------
 

@@ -198,6 +198,29 @@ def main():
     if ar.status() != 0:
         fail(f"fused status {ar.status()}")
 
+    # 3c. the same layer with the decoder layer's residual add + RMSNorm in the epilogue:
+    # bit-identical on every rank, the residual updated in place, and equal to the oracle's norm
+    # of the plain fused output (new residual bit for bit, output within two fp16 ulps)
+    gn = torch.Generator(device="cuda").manual_seed(55)  # the same residual on every rank
+    res0 = (torch.randn(M, N, device="cuda", generator=gn) * 4).half()
+    wn = (1.0 + (torch.rand(N, device="cuda", generator=gn) - 0.5) * 0.4).half()
+    rn = res0.clone()
+    yn = ar.w4_gemm_all_reduce_rmsnorm(xs, qws, qzs, scs, rn, wn, 1e-6)
+    torch.cuda.synchronize()
+    same_y, same_res = gather_equal(yn), gather_equal(rn)  # both collectives on every rank
+    if not (same_y and same_res):
+        fail("fused GEMM+all-reduce+RMSNorm results differ across ranks")
+    if r == 0:
+        ref_out, ref_res = so.add_rmsnorm_ref(yf.cpu().numpy(), res0.cpu().numpy(),
+                                              wn.cpu().numpy(), 1e-6)
+        if not np.array_equal(rn.cpu().numpy().view(np.int16), ref_res.view(np.int16)):
+            fail("fused RMSNorm: residual differs from the oracle")
+        ulp = so.fp16_ulp_distance(yn.cpu().numpy(), ref_out)
+        if ulp.max() > 2 or (ulp == 0).mean() < 0.99:
+            fail(f"fused RMSNorm: max ulp {ulp.max()}, exact {(ulp == 0).mean():.5f}")
+    if ar.status() != 0:
+        fail(f"fused RMSNorm status {ar.status()}")
+
     # 3b. the same layer through the other split-K kernel's fused epilogue (the default is the
     # cluster kernel; B2_TUNE_W4_PATH = 1 selects stream-K with its global fix-up)
     from mi50_vllm_lab_b200 import capi
@@ -225,6 +248,8 @@ def main():
     # 4. timings (max over ranks): fused vs GEMM + NCCL, and the bare all-reduce vs NCCL at 80 KB
     a80 = torch.randn(8 * 5120, device="cuda", dtype=torch.float16, generator=g)
     t_fused = graph_time_us(lambda: ar.w4_gemm_all_reduce(xs, qws, qzs, scs))
+    t_fused_norm = graph_time_us(
+        lambda: ar.w4_gemm_all_reduce_rmsnorm(xs, qws, qzs, scs, rn, wn, 1e-6))
 
     def unfused():
         yy = ops.w4gemm(xs, qws, qzs, scs, 0, 0)
@@ -257,6 +282,7 @@ def main():
         print(json.dumps({"world": P, "config": f"3: down_proj K={K} sharded {P} ways, M={M}, N={N}",
                           "fused_us": round(t_fused, 2),
                           "fused_streamk_us": round(t_fused_streamk, 2),
+                          "fused_with_rmsnorm_us": round(t_fused_norm, 2),
                           "gemm_plus_nccl_us": round(t_unfused, 2),
                           "gemm_only_us": round(t_gemm, 2), "nvlink_ar_80KB_us": round(t_ar, 2),
                           "nccl_ar_80KB_us": round(t_nccl, 2),

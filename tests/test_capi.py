@@ -110,6 +110,9 @@ def test_allreduce_rejects_bad_arguments(capi):
     assert lib.b2_nvar_create(0, 0, 9, 1024, C.byref(out)) == capi.B2_ERR_INVALID_ARG
     assert lib.b2_w4_gemm_allreduce(None, _ALIGNED, _ALIGNED, _ALIGNED, _ALIGNED, _ALIGNED, 4, 512,
                                     256, 128, _ALIGNED, 1 << 30, None) == capi.B2_ERR_STATE
+    assert lib.b2_w4_gemm_allreduce_rmsnorm(None, _ALIGNED, _ALIGNED, _ALIGNED, _ALIGNED, _ALIGNED,
+                                            _ALIGNED, 1e-6, _ALIGNED, 4, 512, 256, 128, _ALIGNED,
+                                            1 << 30, None) == capi.B2_ERR_STATE
 
 
 def test_tuning_knobs(capi):

@@ -10,10 +10,54 @@ from conftest import GOLDEN
 
 W4_GOLDEN = sorted(GOLDEN.glob("w4_*.npz"))
 F16_GOLDEN = sorted(GOLDEN.glob("f16_*.npz"))
+NORM_GOLDEN = sorted(GOLDEN.glob("rmsnorm_*.npz"))
 
 
 def test_golden_files_present():
-    assert len(W4_GOLDEN) >= 7 and len(F16_GOLDEN) >= 4
+    assert len(W4_GOLDEN) >= 7 and len(F16_GOLDEN) >= 4 and len(NORM_GOLDEN) >= 4
+
+
+@pytest.mark.parametrize("path", NORM_GOLDEN, ids=lambda p: p.stem)
+def test_add_rmsnorm_oracle_matches_vllm(oracle, path):
+    """The restated residual add + RMSNorm against vLLM 0.22.0's own fused_add_rms_norm: the new
+    residual bit for bit; the output within one fp16 ulp (the oracle takes the mean and rsqrt
+    in float64, torch in float32), equal almost everywhere."""
+    d = np.load(path)
+    out, res = oracle.add_rmsnorm_ref(d["y"], d["residual"], d["weight"], float(d["eps"]))
+    assert np.array_equal(res.view(np.int16), d["new_residual"].view(np.int16))
+    ulp = oracle.fp16_ulp_distance(out, d["out"])
+    assert ulp.max() <= 1 and (ulp == 0).mean() >= 0.999, (ulp.max(), (ulp == 0).mean())
+    assert np.isfinite(out).all()
+
+
+def test_add_rmsnorm_oracle_invariants(oracle):
+    rng = np.random.default_rng(5)
+    y = (rng.standard_normal((3, 512)) * 3).astype(np.float16)
+    r = rng.standard_normal((3, 512)).astype(np.float16)
+    ones = np.ones(512, np.float16)
+    out, res = oracle.add_rmsnorm_ref(y, r, ones, 1e-6)
+    # unit weight: each output row has mean square 1 (up to fp16 rounding)
+    ms = (out.astype(np.float64) ** 2).mean(axis=1)
+    np.testing.assert_allclose(ms, 1.0, rtol=2e-3)
+    # the norm is scale-invariant up to rounding: scaling y and the residual by 2 (exact in
+    # fp16) leaves the output unchanged, and doubles the new residual exactly
+    out2, res2 = oracle.add_rmsnorm_ref(y * np.float16(2), r * np.float16(2), ones, 0.0)
+    out1, _ = oracle.add_rmsnorm_ref(y, r, ones, 0.0)
+    assert np.array_equal(out1, out2)
+    assert np.array_equal(res2, res * np.float16(2))
+    # a zero row gives zeros (eps keeps the scale finite)
+    z = np.zeros((1, 64), np.float16)
+    o0, _ = oracle.add_rmsnorm_ref(z, z, ones[:64], 1e-6)
+    assert not o0.any() and np.isfinite(o0).all()
+
+
+def test_fp16_ulp_distance(oracle):
+    one = np.float16(1)
+    nxt = np.nextafter(one, np.float16(2))
+    assert oracle.fp16_ulp_distance(np.array([one, -0.0], np.float16),
+                                    np.array([nxt, 0.0], np.float16)).tolist() == [1, 0]
+    assert oracle.fp16_ulp_distance(np.array([-nxt], np.float16),
+                                    np.array([-one], np.float16)).tolist() == [1]
 
 
 @pytest.mark.parametrize("path", W4_GOLDEN, ids=lambda p: p.stem)
