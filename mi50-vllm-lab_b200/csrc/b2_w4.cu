@@ -1390,7 +1390,13 @@ int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* q
     args.nw = static_cast<const __half*>(nw);
     args.npart = reinterpret_cast<float*>(static_cast<char*>(ws) + ws_norm_offset());
   }
-  return dispatch<true>(args, qw, qz, sc, &v, stream, kWsMaxCtas, /*early=*/true);
+  // The RMSNorm epilogue's grid-wide barrier needs every CTA resident at once, so that launch
+  // starts only after the previous kernel has finished. Launched early, a grid's first clusters
+  // take whatever slots the previous grid leaves free; measured on B200 with 40 clusters of 12
+  // CTAs (42 fit an idle GPU), fewer than 40 could then be resident together and back-to-back
+  // launches ran their barrier into the timeout. A kernel after this one may still start early:
+  // by then every CTA of this grid is resident.
+  return dispatch<true>(args, qw, qz, sc, &v, stream, kWsMaxCtas, /*early=*/!norm);
 }
 
 }  // namespace b2

@@ -110,6 +110,34 @@ def test_fused_rmsnorm_matches_oracle(capi, handle, ws, oracle, path, M, K, N, G
         lib.b2_set_tuning(4, saved)
 
 
+def test_back_to_back_launches(capi, handle, ws, oracle):
+    """Eight launches in a row on one stream (40 clusters of 12 CTAs each, near the 42 that fit
+    the GPU), with a 500 ms bound on the grid-wide barrier: none may give up (status 0), and each
+    normalises the residual the previous one left, as the oracle does."""
+    lib = capi.lib()
+    M, K, N, G = 8, 4352, 5120, 128
+    x, qw, qz, sc, res0, w = layer_inputs(oracle, M, K, N, G, seed=21)
+    dx, dqw, dqz, dsc, dw = dev(x), dev(qw), dev(qz), dev(sc), dev(w)
+    y_ar = fused_ar(capi, handle, ws, dx, dqw, dqz, dsc, M, K, N, G).cpu().numpy()
+    capi.check(lib.b2_nvar_set_timeout_ns(handle, 500_000_000), "set_timeout")
+    try:
+        r = dev(res0)
+        outs = [fused_norm(capi, handle, ws, dx, dqw, dqz, dsc, r, dw, M, K, N, G)
+                for _ in range(8)]
+        torch.cuda.synchronize()
+        st = C.c_int(-1)
+        capi.check(lib.b2_nvar_status(handle, 1, C.byref(st)), "nvar_status")
+        assert st.value == 0, f"a grid-wide barrier gave up (status {st.value})"
+    finally:
+        capi.check(lib.b2_nvar_set_timeout_ns(handle, 10_000_000_000), "set_timeout")
+    res = res0
+    for i, out in enumerate(outs):
+        ref_out, res = oracle.add_rmsnorm_ref(y_ar, res, w, EPS)
+        ulp = oracle.fp16_ulp_distance(out.cpu().numpy(), ref_out)
+        assert ulp.max() <= 2 and (ulp == 0).mean() >= 0.99, (i, ulp.max(), (ulp == 0).mean())
+    assert np.array_equal(r.cpu().numpy().view(np.int16), res.view(np.int16))
+
+
 def test_fused_rmsnorm_edge_rows(capi, handle, ws, oracle):
     """A zero row (the residual cancels the layer output: x = 0, eps alone sets the scale) and
     large values (sum of squares far beyond fp16 range) in one call."""
