@@ -625,6 +625,9 @@ def run_norm_epilogue(args):
     import __graft_entry__ as entry
 
     ops = entry.load_package().ops()
+    from mi50_vllm_lab_b200 import capi
+
+    lib = capi.lib()
     torch.cuda.set_device(0)
     M, N, G, eps = 8, CFG4["hidden"], CFG4["G"], 1e-6
     name = f"/b2_bench_norm_{os.getpid()}"
@@ -664,6 +667,8 @@ def run_norm_epilogue(args):
             r = res0.clone()
             variants = {
                 "gemm_ar": lambda t: ops.w4gemm_ar(x, *t, h),
+                # the same launch without early start, as the norm epilogue is launched
+                "gemm_ar_no_early_launch": lambda t: ops.w4gemm_ar(x, *t, h),
                 "gemm_ar_norm_fused": lambda t: ops.w4gemm_ar_rmsnorm(x, *t, h, r, w, eps),
                 "gemm_ar_then_torch_norm": lambda t: torch_norm(ops.w4gemm_ar(x, *t, h), r),
             }
@@ -677,6 +682,8 @@ def run_norm_epilogue(args):
                    "l2_rotation_copies": copies}
             for vname, fn in variants.items():
                 reps = max(copies, min(64, 20 * copies)) // copies * copies
+                capi.check(lib.b2_set_tuning(3, 1 if vname == "gemm_ar_no_early_launch" else 0),
+                           "b2_set_tuning")  # B2_TUNE_NO_PDL, read at launch (and capture) time
                 try:
                     for t in ws:
                         fn(t)
@@ -707,6 +714,7 @@ def run_norm_epilogue(args):
                     times.append(e0.elapsed_time(e1) * 1e3 / reps)
                 row[vname + "_us"] = round(statistics.median(times), 2)
                 del graph
+            capi.check(lib.b2_set_tuning(3, 0), "b2_set_tuning")
             row["status"] = int(ops.nvar_status(h, False))
             print(json.dumps(row), flush=True)
             del ws

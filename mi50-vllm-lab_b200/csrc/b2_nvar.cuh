@@ -26,15 +26,27 @@ constexpr size_t kArHeaderBytes = 4096;
 constexpr size_t kArFlagsBytes = (size_t)kArMaxWorld * kArMaxFlags * sizeof(uint32_t);
 constexpr size_t kArSlotsOffset = kArHeaderBytes + kArFlagsBytes;
 
+// Grid-wide barrier of a fused launch that normalises rows (residual add + RMSNorm): CTA b
+// arrives on sub-counter b % kNormFanout; the last CTA of each sub-counter arrives on the top
+// counter; the last of those releases the launch's generation in norm_gen. The flag and every
+// counter sit on their own 128-byte line, so the waiters' polling does not slow the arrivals.
+constexpr int kNormFanout = 16;
+
 struct ArHeader {
   uint32_t gen;   // completed launches
   uint32_t done;  // CTAs of the running launch that finished
   int status;     // 0 or B2_ERR_TIMEOUT
-  // grid-wide barrier of a fused launch that normalises rows (residual add + RMSNorm): CTAs
-  // arrived so far, and the generation of the last launch whose CTAs all arrived
-  uint32_t norm_count;
-  uint32_t norm_gen;
+  uint32_t pad0[29];
+  uint32_t norm_gen;  // generation of the last launch whose CTAs all arrived
+  uint32_t pad1[31];
+  uint32_t norm_top;  // sub-counters complete so far
+  uint32_t pad2[31];
+  struct {
+    uint32_t count;  // CTAs arrived so far
+    uint32_t pad[31];
+  } norm_sub[kNormFanout];
 };
+static_assert(sizeof(ArHeader) <= kArHeaderBytes, "the header must fit its 4 KB");
 
 // Kernel-parameter view of one all-reduce handle.
 struct ArView {
