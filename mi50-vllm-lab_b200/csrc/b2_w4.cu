@@ -276,14 +276,51 @@ __device__ __forceinline__ bool norm_rstd(const W4Args& p, const ArView& ar, uin
   named_bar_sync(1, kWarps * 32);
   __threadfence();
   const bool ok = *s_flag != 0;
-  // rstd of row m (warp m % 4): lane l adds the sums of CTAs l, l + 32, ... in order, then a
-  // fixed shuffle tree
-  for (int m = warp; m < p.M; m += kWarps) {
-    float v = 0.f;
-    for (int b = lane; b < (int)gridDim.x; b += 32) v += __ldcg(p.npart + (size_t)b * kMaxM + m);
+  // All CTAs' row sums: thread i takes CTAs i, i + 128, ... (both 16-byte halves of each CTA's
+  // eight sums, four CTAs' loads in flight at a time), adds them in that order, then the same
+  // fixed shuffle tree and warp order as above. Every CTA runs the same sequence on the same
+  // data, so every CTA gets the same sums.
+  float acc[kMaxM];
+#pragma unroll
+  for (int m = 0; m < kMaxM; ++m) acc[m] = 0.f;
+  const int nb = (int)gridDim.x;
+  for (int b0 = tid; b0 < nb; b0 += 4 * kWarps * 32) {
+    float4 lo[4], hi[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int b = b0 + j * kWarps * 32;
+      if (b < nb) {
+        lo[j] = __ldcg(reinterpret_cast<const float4*>(p.npart + (size_t)b * kMaxM));
+        hi[j] = __ldcg(reinterpret_cast<const float4*>(p.npart + (size_t)b * kMaxM + 4));
+      } else {
+        lo[j] = hi[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[0] += lo[j].x;
+      acc[1] += lo[j].y;
+      acc[2] += lo[j].z;
+      acc[3] += lo[j].w;
+      acc[4] += hi[j].x;
+      acc[5] += hi[j].y;
+      acc[6] += hi[j].z;
+      acc[7] += hi[j].w;
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < kMaxM; ++m) {
+    float v = acc[m];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) s_norm[kWarps * kMaxM + m] = rsqrtf(v / (float)p.N + p.eps);
+    if (lane == 0) s_norm[warp * kMaxM + m] = v;
+  }
+  named_bar_sync(1, kWarps * 32);
+  if (tid < p.M) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) v += s_norm[w * kMaxM + tid];
+    s_norm[kWarps * kMaxM + tid] = rsqrtf(v / (float)p.N + p.eps);
   }
   named_bar_sync(1, kWarps * 32);
   return ok;
