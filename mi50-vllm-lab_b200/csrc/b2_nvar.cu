@@ -268,8 +268,7 @@ int b2_nvar_status(b2_nvar* h, int clear, int* device_status) {
   if (clear && hdr.status) {
     B2_CUDA_TRY(cudaMemset(h->local + offsetof(ArHeader, status), 0, sizeof(int)));
     // a launch that gave up may have left CTAs counted at its grid-wide barrier
-    B2_CUDA_TRY(cudaMemset(h->local + offsetof(ArHeader, norm_top), 0,
-                           sizeof(ArHeader) - offsetof(ArHeader, norm_top)));
+    B2_CUDA_TRY(cudaMemset(h->local + offsetof(ArHeader, norm_count), 0, sizeof(uint32_t)));
   }
   *device_status = hdr.status;
   return B2_OK;

@@ -26,12 +26,10 @@ constexpr size_t kArHeaderBytes = 4096;
 constexpr size_t kArFlagsBytes = (size_t)kArMaxWorld * kArMaxFlags * sizeof(uint32_t);
 constexpr size_t kArSlotsOffset = kArHeaderBytes + kArFlagsBytes;
 
-// Grid-wide barrier of a fused launch that normalises rows (residual add + RMSNorm): CTA b
-// arrives on sub-counter b % kNormFanout; the last CTA of each sub-counter arrives on the top
-// counter; the last of those releases the launch's generation in norm_gen. The flag and every
-// counter sit on their own 128-byte line, so the waiters' polling does not slow the arrivals.
-constexpr int kNormFanout = 16;
-
+// norm_count / norm_gen: the grid-wide barrier of a fused launch that normalises rows (residual
+// add + RMSNorm). Every CTA adds 1 to norm_count; the last one resets it and stores the launch's
+// generation in norm_gen, which the others wait for. Each sits on its own 128-byte line, so the
+// waiters' polling does not slow the arrivals.
 struct ArHeader {
   uint32_t gen;   // completed launches
   uint32_t done;  // CTAs of the running launch that finished
@@ -39,12 +37,8 @@ struct ArHeader {
   uint32_t pad0[29];
   uint32_t norm_gen;  // generation of the last launch whose CTAs all arrived
   uint32_t pad1[31];
-  uint32_t norm_top;  // sub-counters complete so far
+  uint32_t norm_count;  // CTAs of the running launch that arrived
   uint32_t pad2[31];
-  struct {
-    uint32_t count;  // CTAs arrived so far
-    uint32_t pad[31];
-  } norm_sub[kNormFanout];
 };
 static_assert(sizeof(ArHeader) <= kArHeaderBytes, "the header must fit its 4 KB");
 

@@ -238,29 +238,19 @@ __device__ __forceinline__ bool norm_rstd(const W4Args& p, const ArView& ar, uin
     p.npart[(size_t)blockIdx.x * kMaxM + tid] = v;
   }
   named_bar_sync(1, kWarps * 32);
-  // grid-wide barrier (a two-level arrival tree, see ArHeader): the last CTA of a sub-counter
-  // resets it and arrives on the top counter; the last of those resets that and releases
-  // generation e. The fence before each arrival makes what the CTA (or, through the earlier
-  // arrivals it observed, the CTAs before it) wrote visible to whoever observes the arrival.
+  // grid-wide barrier: the last CTA to arrive resets the count and releases generation e (the
+  // release orders the reset before the store). The fence before each arrival makes the CTA's
+  // row sums, ordered before it by the CTA barrier, visible to whoever observes the arrival;
+  // a CTA's other threads see the released sums through the CTA barrier after thread 0's
+  // acquire.
   if (tid == 0) {
     ArHeader* h = ar_header(ar);
-    const unsigned nb = gridDim.x;
-    const unsigned fan = nb < (unsigned)kNormFanout ? nb : (unsigned)kNormFanout;
-    const unsigned sub = blockIdx.x % fan;
-    const unsigned n_sub = (nb - sub + fan - 1) / fan;  // CTAs b < nb with b % fan == sub
-    bool ok = true, released = false;
+    bool ok = true;
     __threadfence();
-    if (atomicAdd(&h->norm_sub[sub].count, 1u) == n_sub - 1) {
-      atomicExch(&h->norm_sub[sub].count, 0u);
-      __threadfence();
-      if (atomicAdd(&h->norm_top, 1u) == fan - 1) {
-        atomicExch(&h->norm_top, 0u);
-        __threadfence();
-        st_release_sys(&h->norm_gen, e);
-        released = true;
-      }
-    }
-    if (!released) {
+    if (atomicAdd(&h->norm_count, 1u) == gridDim.x - 1) {
+      atomicExch(&h->norm_count, 0u);
+      st_release_sys(&h->norm_gen, e);
+    } else {
       const unsigned long long t0 = globaltimer_ns();
       unsigned int it = 0;
       while ((int)(ld_acquire_sys(&h->norm_gen) - e) < 0) {
@@ -268,13 +258,12 @@ __device__ __forceinline__ bool norm_rstd(const W4Args& p, const ArView& ar, uin
           ok = false;
           break;
         }
-        __nanosleep(64);
+        __nanosleep(32);
       }
     }
     *s_flag = ok ? 1 : 0;
   }
   named_bar_sync(1, kWarps * 32);
-  __threadfence();
   const bool ok = *s_flag != 0;
   // All CTAs' row sums: thread i takes CTAs i, i + 128, ... (both 16-byte halves of each CTA's
   // eight sums, four CTAs' loads in flight at a time), adds them in that order, then the same
