@@ -188,7 +188,9 @@ int b2_nvar_allreduce(b2_nvar* ar, const void* in, void* out, size_t count, int 
                       void* stream);
 /* Row-parallel W4A16 layer: y = allreduce_over_ranks(a_rank @ dequant(qw_rank, ...)), with the
  * all-reduce fused into the GEMM epilogue. Each rank passes its K-shard; M, N, G match on all
- * ranks. fp32 partials cross NVLink; the fp16 result is bit-identical on every rank. */
+ * ranks, and so does the tuning (the ranks must choose the same split-K plan). The fp32 partial
+ * sums cross NVLink as 64-bit (generation, value) words; they are added in rank order, so the
+ * fp16 result is bit-identical on every rank. The handle's slot must hold M * N * 4 bytes. */
 int b2_w4_gemm_allreduce(b2_nvar* ar, const void* a, const void* qw, const void* qz,
                          const void* sc, void* y, int M, int K, int N, int group_size, void* ws,
                          size_t ws_bytes, void* stream);

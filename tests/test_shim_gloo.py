@@ -80,6 +80,22 @@ class FakeOps:
     def nvar_status(self, handle, clear):
         return 0
 
+    def w4gemm_ar(self, x, w_q, w_zp, w_s, handle):
+        """This rank's K-shard GEMM as an fp32 partial, summed over ranks in rank order and
+        rounded once (the fused kernel's contract)."""
+        from oracle import skinny_oracle as so
+
+        part = so.w4_ref(x.numpy(), w_q.numpy(), w_zp.numpy(), w_s.numpy()).astype("float32")
+        return self._sum(torch.from_numpy(part)).half()
+
+    def w4gemm_ar_rmsnorm(self, x, w_q, w_zp, w_s, handle, residual, weight, eps):
+        from oracle import skinny_oracle as so
+
+        y = self.w4gemm_ar(x, w_q, w_zp, w_s, handle)
+        out, res = so.add_rmsnorm_ref(y.numpy(), residual.numpy(), weight.numpy(), eps)
+        residual.copy_(torch.from_numpy(res))
+        return torch.from_numpy(out)
+
 
 def _worker(rank, world, port, scenario, result_q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -116,6 +132,30 @@ def _worker(rank, world, port, scenario, result_q):
             assert not ar.should_use(torch.zeros(1 << 17, dtype=torch.float16))  # > max bytes
             if rank == 0:
                 assert len(fake.unlinked) == 1
+            # row-parallel layer + residual add + RMSNorm through the shim: every rank passes
+            # its K-shard and the same residual; the residual is updated in place, every rank
+            # gets the same result, and it matches the unsharded layer's oracle
+            M, ks, N, G = 4, 256, 128, 128
+            x, qw, qz, sc = so.gen_w4(M, ks * world, N, G, seed=3)
+            xs = torch.from_numpy(x[:, rank * ks:(rank + 1) * ks].copy())
+            qws = torch.from_numpy(qw[rank * ks // 8:(rank + 1) * ks // 8].copy())
+            qzs = torch.from_numpy(qz[rank * ks // G:(rank + 1) * ks // G].copy())
+            scs = torch.from_numpy(sc[rank * ks // G:(rank + 1) * ks // G].copy())
+            gr = torch.Generator().manual_seed(9)
+            res0 = (torch.randn(M, N, generator=gr) * 2).half()
+            wn = (1 + torch.rand(N, generator=gr) * 0.2).half()
+            res = res0.clone()
+            out = ar.w4_gemm_all_reduce_rmsnorm(xs, qws, qzs, scs, res, wn, 1e-6)
+            assert not torch.equal(res, res0)  # updated in place
+            for t in (out, res):
+                parts = [torch.empty_like(t) for _ in range(world)]
+                dist.all_gather(parts, t)
+                assert all(torch.equal(parts[0], q) for q in parts[1:])
+            y_full = so.w4_ref(x, qw, qz, sc).astype("float16")
+            ref_out, ref_res = so.add_rmsnorm_ref(y_full, res0.numpy(), wn.numpy(), 1e-6)
+            # the sharded fp32 partials and the float64 full GEMM round apart by an ulp at most
+            assert so.fp16_ulp_distance(res.numpy(), ref_res).max() <= 1
+            assert so.fp16_ulp_distance(out.numpy(), ref_out).max() <= 3
             result_q.put((rank, "ok"))
         else:  # rank 1 never publishes its buffer: rank 0's connect must raise, not hang
             fake = FakeOps(lib, join=(rank == 0))
