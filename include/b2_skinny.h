@@ -205,7 +205,9 @@ int b2_w4_gemm_allreduce(b2_nvar* ar, const void* a, const void* qw, const void*
  * y, residual and norm_weight must not overlap. 0 <= eps <= 1. The row sums are added in a fixed
  * order, so y and residual are bit-identical on every rank and from call to call. One
  * grid-wide barrier inside the kernel (bounded by the handle's timeout; B2_ERR_TIMEOUT in the
- * handle's status if it gives up). */
+ * handle's status if it gives up). The barrier needs all of the launch's CTAs resident at once,
+ * so this launch never starts early (no programmatic dependent launch), and kernels that other
+ * streams keep running on the GPU for its whole duration can make it time out. */
 int b2_w4_gemm_allreduce_rmsnorm(b2_nvar* ar, const void* a, const void* qw, const void* qz,
                                  const void* sc, void* residual, const void* norm_weight,
                                  float eps, void* y, int M, int K, int N, int group_size,
