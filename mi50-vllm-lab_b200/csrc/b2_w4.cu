@@ -23,7 +23,8 @@
 //     access to activations, workspace and y comes after that wait.
 //   - optionally the NVLink all-reduce of a row-parallel layer is fused into the epilogue: the
 //     finished fp32 tile is pushed to every rank, and each rank adds the ranks' tiles in rank
-//     order (bit-identical on every rank).
+//     order (bit-identical on every rank); and optionally, after it, the decoder layer's
+//     residual add + RMSNorm (row sums through one grid-wide barrier, see norm_rstd).
 #include <cuda_fp16.h>
 
 #include <algorithm>
