@@ -86,7 +86,9 @@ def run_f16(root: Path, x, w):
 
 
 def main() -> None:
-    root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/mi50-vllm-lab")
+    root = Path(sys.argv[1])
     torch.set_num_threads(1)
     for name, M, K, N, G, seed, xs in W4_CASES:
         x, qw, qz, sc = so.gen_w4(M, K, N, G, seed, x_scale=xs)
