@@ -1,18 +1,29 @@
 """Benchmark of the skinny-GEMM hot path on B200.
 
-Default (the driver's line): BASELINE config 1, the fp16 skinny GEMM at lm_head shape
-M=7, K=5120, N=151936 (1.56 GB of weights, larger than the 126 MB L2, so no flush is needed).
-One step = one GEMM through the C ABI on device-resident operands. With N GPUs (torchrun, one
-rank per GPU) every rank runs its own config-1 GEMM (weak scaling; column-parallel shards need no
-collective); `value` is the aggregate HBM throughput of all ranks, timed as the max over ranks.
+Default (the driver's line): BASELINE config 4, the synthetic decode-verify step of a 64-layer
+W4A16 model at M = 8 (speculative k = 7), tensor parallel over the N ranks (TP = N, one process
+per GPU under torchrun): per layer qkv_proj and gate_up (column-parallel, N-sharded) and o_proj
+and down_proj (row-parallel, K-sharded, with the NVLink all-reduce fused into the GEMM epilogue
+when N > 1), then the fp16 lm_head (column-parallel). All 257 launches of a step are captured in
+one CUDA graph; one step = one replay. `value` is microseconds per step, timed on the device with
+CUDA events and taken as the max over ranks. The line also carries:
+  * `roofline`: the kernel that takes most of the step, timed alone (a graph of its 64 launches
+    of the step, CUDA events), against its algorithmic bytes and the measured HBM peak;
+  * `kernels`: the same per-launch figures for every kind of launch of the step;
+  * `e2e`: the step through the operator library with the step's input activations copied from
+    pinned host memory and the logits copied back, every step;
+  * `cpu_baseline` (N = 1): the reference's CPU path (torch dequantize-then-matmul,
+    kernels/check_w4.py:11-21; `x.float() @ w.float().T`, kernels/bench_skinny.py:44) timed on
+    the host cores over a column sample of every GEMM of one layer and a row sample of the
+    lm_head, scaled to a full step;
+  * `extra` (N = 1): config 1 (fp16 lm_head GEMM) and config 0 (W4 4096 x 4096) on their own, as
+    in the earlier default line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-    python bench.py --impl reference      # the reference's CPU path (torch dequant+matmul)
-    python bench.py --sweep               # every BASELINE config, one JSON line each (not timed by the driver)
+    python bench.py --impl reference      # the reference's CPU path on the same step and metric
+    python bench.py --sweep               # every single-GEMM BASELINE config, one JSON line each
+    python bench.py --config1             # config 1 alone (fp16 lm_head GEMM, TB/s)
     python bench.py --norm-epilogue       # row-parallel layer + residual add + RMSNorm, fused vs separate
-
-Metric: HBM TB/s of algorithmic bytes (2*N*K + 2*M*K + 2*M*N for fp16; the W4 formula for W4),
-and us per GEMM.
 """
 
 from __future__ import annotations
@@ -29,9 +40,12 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-METRIC = "W4A16/fp16 skinny-GEMM HBM throughput at M<=8 (config 1: fp16 lm_head GEMM)"
-UNIT = "TB/s"
+METRIC = ("W4A16/fp16 skinny-GEMM decode-verify step, config 4 (64 W4A16 layers + fp16 lm_head, "
+          "M=8, TP=N with the all-reduce fused into the row-parallel GEMMs): us per step")
+UNIT = "us"
 CFG1 = dict(M=7, K=5120, N=151936)
+CFG0 = dict(M=7, K=4096, N=4096, G=128)
+CFG4 = dict(layers=64, M=8, hidden=5120, qkv=8192, o_in=6144, inter=17408, vocab=151936, G=128)
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -64,8 +78,19 @@ def recorded_traffic(kernel: str, workload: str):
         return None
 
 
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML while the timed region runs."""
+    """Samples SM clock and clock-event reasons through NVML while the timed region runs
+    (every millisecond by default)."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -73,7 +98,7 @@ class ClockSampler:
         0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
     }
 
-    def __init__(self, index: int, period_s: float = 0.01):
+    def __init__(self, index: int, period_s: float = 0.001):
         self.samples, self.reasons = [], set()
         self.max_mhz = None
         self._stop = threading.Event()
@@ -118,7 +143,8 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
                     "samples": 0}
         return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples),
+                "period_ms": self.period * 1e3}
 
 
 # ------------------------------------------------------------------------------------------------
@@ -169,26 +195,6 @@ def max_over_ranks(v: float, world: int) -> float:
     return float(t.item())
 
 
-# ------------------------------------------------------------------------------------------------
-# CPU baseline: the reference's own torch path (kernels/bench_skinny.py:44; kernels/check_w4.py)
-# ------------------------------------------------------------------------------------------------
-
-
-def cpu_baseline_f16(x_cpu, w_rows_cpu, budget_s: float = 10.0):
-    """Time `x.float() @ w.float().T` (the reference's fp16 GEMM reference) on the host cores
-    over a row sample of the weights; returns (TB/s, seconds per call, cores, description)."""
-    import torch
-
-    from oracle import cpu_baseline
-
-    return cpu_baseline.time_f16(x_cpu, w_rows_cpu, budget_s=budget_s)
-
-
-# ------------------------------------------------------------------------------------------------
-# GPU legs
-# ------------------------------------------------------------------------------------------------
-
-
 def time_steps(fn, steps: int, world: int, stream):
     """Time exactly `steps` calls of fn between barriers with one pair of CUDA events on `stream`
     around all of them (events between the steps would put gaps between the launches)."""
@@ -204,6 +210,203 @@ def time_steps(fn, steps: int, world: int, stream):
     return start.elapsed_time(end)
 
 
+def capture(fn):
+    """Capture fn() in a CUDA graph on a side stream; returns (graph, fn's return value)."""
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            out = fn()
+    torch.cuda.current_stream().wait_stream(s)
+    return graph, out
+
+
+# ------------------------------------------------------------------------------------------------
+# BASELINE config 4: the decode-verify step
+# ------------------------------------------------------------------------------------------------
+
+
+def decode_step_bytes(P: int) -> int:
+    """Algorithmic HBM bytes one rank moves per step at TP = P."""
+    c = CFG4
+    return c["layers"] * sum(w4_bytes(c["M"], K, N, c["G"]) for K, N in layer_shapes(P).values()) \
+        + f16_bytes(c["M"], c["hidden"], c["vocab"] // P)
+
+
+def layer_shapes(P: int) -> dict:
+    """(K, N) of this rank's four W4 GEMMs per layer at TP = P."""
+    c = CFG4
+    return {"qkv": (c["hidden"], c["qkv"] // P), "o": (c["o_in"] // P, c["hidden"]),
+            "gate_up": (c["hidden"], 2 * c["inter"] // P), "down": (c["inter"] // P, c["hidden"])}
+
+
+class DecodeModel:
+    """Random-initialised weights of one rank's shard of config 4 and the step that runs them
+    through torch.ops.gfx906_skinny (the operators vLLM calls)."""
+
+    def __init__(self, ops, P: int, rank: int, ar, seed: int = 4000):
+        import torch
+
+        c = CFG4
+        self.ops, self.ar, self.P = ops, ar, P
+        M, H, G = c["M"], c["hidden"], c["G"]
+        g = torch.Generator(device="cuda").manual_seed(seed + rank)
+        sh = layer_shapes(P)
+
+        def w4(K, N):
+            return (torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32,
+                                  generator=g),
+                    torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda",
+                                  dtype=torch.int32, generator=g),
+                    (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half())
+
+        self.layers = [{k: w4(*sh[k]) for k in ("qkv", "o", "gate_up", "down")}
+                       for _ in range(c["layers"])]
+        self.lm = (torch.randn(c["vocab"] // P, H, device="cuda", generator=g) * 0.02).half()
+        self.x0 = torch.randn(M, H, device="cuda", generator=g).half()
+        # attention output and activated MLP input of this rank's shard (synthetic, fixed: the
+        # attention and the activation are not part of this path)
+        self.a_o = (torch.randn(M, c["o_in"] // P, device="cuda", generator=g) * 0.05).half()
+        self.a_d = (torch.randn(M, c["inter"] // P, device="cuda", generator=g) * 0.05).half()
+
+    def row_parallel(self, a, w):
+        return self.ar.w4_gemm_all_reduce(a, *w) if self.ar else self.ops.w4gemm(a, *w, 0, 0)
+
+    def launch(self, kind: str, L: dict, h):
+        if kind in ("o", "down"):
+            return self.row_parallel(self.a_o if kind == "o" else self.a_d, L[kind])
+        return self.ops.w4gemm(h, *L[kind], 0, 0)
+
+    def step(self):
+        h = self.x0
+        for L in self.layers:
+            self.launch("qkv", L, h)
+            h = self.launch("o", L, h)
+            self.launch("gate_up", L, h)
+            h = self.launch("down", L, h)
+        return self.ops.gemm(h, self.lm, 0)
+
+    def kind_step(self, kind: str):
+        """The step's launches of one kind only (64 of a layer kind, or 8 lm_head launches)."""
+        if kind == "lm_head":
+            for _ in range(8):
+                self.ops.gemm(self.x0, self.lm, 0)
+            return
+        for L in self.layers:
+            self.launch(kind, L, self.x0)
+
+
+def kernel_breakdown(model: DecodeModel, world: int, capi, reps: int = 5) -> dict:
+    """Per-launch device time of every kind of launch of the step: a graph of that kind's launches
+    (the step's own weights, so every launch reads HBM), replayed `reps` times between CUDA
+    events, max over ranks."""
+    import torch
+
+    c, P = CFG4, model.P
+    st = torch.cuda.current_stream()
+    out = {}
+    for kind in ("qkv", "o", "gate_up", "down", "lm_head"):
+        if kind == "lm_head":
+            K, N, launches = c["hidden"], c["vocab"] // P, 8
+            nb, name = f16_bytes(c["M"], K, N), "gemm_f16_kernel"
+            plan = None
+        else:
+            K, N = layer_shapes(P)[kind]
+            launches = c["layers"]
+            nb = w4_bytes(c["M"], K, N, c["G"])
+            fused = P > 1 and kind in ("o", "down")
+            plan = capi.w4_plan(c["M"], K, N, c["G"], fused)
+            name = plan["kernel"] + ("<fused all-reduce>" if fused else "")
+        graph, _ = capture(lambda: model.kind_step(kind))
+        graph.replay()
+        ms = time_steps(graph.replay, reps, world, st)
+        us = max_over_ranks(ms * 1e3 / (reps * launches), world)
+        del graph
+        out[kind] = {"kernel": name, "K": K, "N": N, "us_per_launch": round(us, 2),
+                     "launches_per_step": 1 if kind == "lm_head" else c["layers"],
+                     "bytes_per_launch": nb}
+        if plan:
+            out[kind]["plan"] = {k: plan[k] for k in ("cluster", "ctas")}
+    return out
+
+
+# ------------------------------------------------------------------------------------------------
+# single-GEMM measurements (--sweep, and the `extra` keys of the default line)
+# ------------------------------------------------------------------------------------------------
+
+
+def measure_gemm(lib, capi, ws, name, kind, M, K, N, G, steps, warmup, peak, l2):
+    """One GEMM shape: launches captured in a CUDA graph that rotates over enough weight copies
+    to exceed 3x L2 (so every launch reads HBM), timed by replaying the graph."""
+    import torch
+
+    wbytes = K * N // 2 if kind == "w4" else 2 * N * K
+    nb = w4_bytes(M, K, N, G) if kind == "w4" else f16_bytes(M, K, N)
+    copies = max(1, int(3 * l2 // wbytes) + 1)
+    g = torch.Generator(device="cuda").manual_seed(M * K + N)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    calls = []
+    for _ in range(copies):
+        if kind == "w4":
+            qw = torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32, generator=g)
+            qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda", dtype=torch.int32, generator=g)
+            sc = (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half()
+            calls.append((qw, qz, sc))
+        else:
+            calls.append((torch.randn(N, K, device="cuda", generator=g) * 0.02).half(),)
+
+    def launch(t, sp):
+        if kind == "w4":
+            qw, qz, sc = t
+            rc = lib.b2_w4_gemm(x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(),
+                                y.data_ptr(), M, K, N, G, ws.data_ptr(), ws.numel(), sp)
+        else:
+            rc = lib.b2_gemm_f16(x.data_ptr(), t[0].data_ptr(), y.data_ptr(), M, K, N,
+                                 ws.data_ptr(), ws.numel(), sp)
+        capi.check(rc, name)
+
+    reps = max(copies, min(64, 20 * copies))
+    reps = (reps // copies) * copies
+    sp0 = torch.cuda.current_stream().cuda_stream
+    for t in calls:
+        launch(t, sp0)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(reps):
+                launch(calls[i % copies], s.cuda_stream)
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    times = []
+    for _ in range(max(3, steps // reps)):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        graph.replay()
+        e1.record(st)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e3 / reps)
+    us = statistics.median(times)
+    del graph
+    return {"workload": name, "kind": kind, "M": M, "K": K, "N": N, "G": G, "us": round(us, 2),
+            "TBps": round(nb / us / 1e6, 3), "frac": round(nb / us / 1e3 / peak, 3),
+            "bytes": nb, "l2_rotation_copies": copies, "launches_per_graph": reps}
+
+
+# ------------------------------------------------------------------------------------------------
+# the default line
+# ------------------------------------------------------------------------------------------------
+
+
 def run_gpu(args):
     import torch
 
@@ -211,86 +414,117 @@ def run_gpu(args):
 
     rank, world, local = dist_setup(args.gpus)
     pkg = entry.load_package()
-    from mi50_vllm_lab_b200 import capi
+    from mi50_vllm_lab_b200 import capi, vllm_shim
 
     ops = pkg.ops()
     lib = capi.lib()
-    M, K, N = CFG1["M"], CFG1["K"], CFG1["N"]
-    nbytes = f16_bytes(M, K, N)
+    c = CFG4
+    M, H, P = c["M"], c["hidden"], world
+    ar = None
+    if P > 1:
+        import datetime
 
-    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
-    x = torch.randn(M, K, device="cuda", generator=g).half()
-    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
-    y = torch.empty(M, N, dtype=torch.float16, device="cuda")
-    ws = torch.zeros(lib.b2_workspace_bytes(local), dtype=torch.uint8, device="cuda")
-    stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
+        import torch.distributed as dist
 
-    def step():
-        rc = lib.b2_gemm_f16(x.data_ptr(), w.data_ptr(), y.data_ptr(), M, K, N, ws.data_ptr(),
-                             ws.numel(), sp)
-        if rc:
-            capi.check(rc, "b2_gemm_f16")
-
+        cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
+        # 8 bytes per output element: room for the low-latency (value + generation) exchange
+        ar = vllm_shim.NvlinkAllReduce(cpu, rank, list(range(P)), slot_bytes=M * H * 8)
+    model = DecodeModel(ops, P, rank, ar)
+    eager = model.step()
+    torch.cuda.synchronize()
+    graph, out = capture(model.step)
     for _ in range(args.warmup):
-        step()
-    with ClockSampler(local) as clk:
-        total_ms = time_steps(step, args.steps, world, stream)
-    ms_step = max_over_ranks(total_ms / args.steps, world)
-    # the timed region holds exactly one launch of the kernel per step: its per-launch period
-    kern_ms = total_ms / args.steps
-    value = world * nbytes / (ms_step * 1e-3) / 1e12
+        graph.replay()
+    torch.cuda.synchronize()
+    same = bool(torch.equal(out, eager))
+    stream = torch.cuda.current_stream()
 
-    # end to end through the plugin API with host buffers: H2D of the activations, the GEMM,
-    # D2H of the logits, every step
-    x_host = torch.randn(M, K, generator=torch.Generator().manual_seed(7)).half().pin_memory()
-    y_host = torch.empty(M, N, dtype=torch.float16).pin_memory()
-    x_dev = torch.empty_like(x)
+    with ClockSampler(local) as clk:
+        total_ms = time_steps(graph.replay, args.steps, world, stream)
+    us_step = max_over_ranks(total_ms * 1e3 / args.steps, world)
+
+    # end to end: the step's input activations from pinned host memory, the graph of operator
+    # calls, the logits back to pinned host memory, every step
+    x_host = torch.randn(M, H, generator=torch.Generator().manual_seed(7)).half().pin_memory()
+    logits_host = torch.empty(out.shape, dtype=torch.float16).pin_memory()
 
     def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
-        out = ops.gemm(x_dev, w, 20)
-        y_host.copy_(out, non_blocking=True)
+        model.x0.copy_(x_host, non_blocking=True)
+        graph.replay()
+        logits_host.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
     e2e_ms = time_steps(e2e_step, args.steps, world, stream)
-    e2e_step_ms = max_over_ranks(e2e_ms / args.steps, world)
-    e2e_value = world * nbytes / (e2e_step_ms * 1e-3) / 1e12
+    e2e_us = max_over_ranks(e2e_ms * 1e3 / args.steps, world)
 
+    kernels = kernel_breakdown(model, world, capi)
+    status = ar.status() if ar else ops.workspace_status(False)
     peak, peak_kind = hbm_peak()
-    achieved = nbytes / (kern_ms * 1e-3) / 1e9
-    clocks = clk.summary()
-    status = ops.workspace_status(False)
-    assert status == 0, f"device status {status}"
+    nbytes = decode_step_bytes(P)
+    for k in kernels.values():
+        k["GBps"] = round(k["bytes_per_launch"] / k["us_per_launch"] / 1e3, 1)
+        k["frac"] = round(k["GBps"] / peak, 4)
+        k["us_per_step"] = round(k["us_per_launch"] * k["launches_per_step"], 1)
+    dom_kind = max(kernels, key=lambda k: kernels[k]["us_per_step"])
+    dom = kernels[dom_kind]
+    del graph
 
     line = None
     if rank == 0:
+        workload = f"config 4 TP={P} {dom_kind}"
         line = {
-            "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "us_per_gemm": round(ms_step * 1e3, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 (fp32 accumulate)", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-            "config": {"workload": "config 1: fp16 skinny GEMM, lm_head shape", "M": M, "K": K,
-                       "N": N, "per_gpu_bytes_per_step": nbytes,
-                       "l2": "weights 1.56 GB > 126 MB L2 (no flush needed)",
-                       "parallelism": f"{world} independent column shards (no collective)"},
-            "e2e": {"value": round(e2e_value, 4), "unit": UNIT, "ms_per_step": round(e2e_step_ms, 5),
-                    "api": "torch.ops.gfx906_skinny.gemm, pinned host x -> device, y -> pinned host",
-                    "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                         "kernel": "gemm_f16_kernel", "kernel_us": round(kern_ms * 1e3, 2),
-                         "traffic": recorded_traffic("gemm_f16_kernel", "config1")},
-            "gpu_launches": args.steps,
-            "clocks": clocks,
+            "metric": METRIC, "value": round(us_step, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us_step / 1e3, 4),
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "W4A16 / f16 (fp32 accumulate)",
+            "data": "synthetic (seeded random int4 weights, U[0.005,0.02] scales, N(0,1) activations)",
+            "config": {"workload": "config 4: decode-verify step, 64 W4A16 layers + fp16 lm_head",
+                       "M": M, "tp": P, "layers": c["layers"], "hidden": H, "qkv": c["qkv"],
+                       "o_in": c["o_in"], "intermediate": c["inter"], "vocab": c["vocab"],
+                       "group_size": c["G"], "kernels_per_step": 4 * c["layers"] + 1,
+                       "fused_allreduces_per_step": 2 * c["layers"] if P > 1 else 0,
+                       "parallelism": f"tp{P}", "per_rank_bytes_per_step": nbytes,
+                       "graph": "one CUDA graph per step; programmatic dependent launch between GEMMs",
+                       "l2": f"each step streams {nbytes / 1e9:.2f} GB of weights per rank "
+                             f"(> 126 MB L2; no flush needed)"},
+            "step_hbm": {"GBps_per_rank": round(nbytes / us_step / 1e3, 1),
+                         "frac": round(nbytes / us_step / 1e3 / peak, 4)},
+            "e2e": {"value": round(e2e_us, 1), "unit": UNIT, "ms_per_step": round(e2e_us / 1e3, 4),
+                    "api": "torch.ops.gfx906_skinny (w4gemm, w4gemm_ar, gemm) captured in one CUDA "
+                           "graph; pinned host x -> device, logits -> pinned host every step",
+                    "h2d_bytes_per_step": M * H * 2, "d2h_bytes_per_step": int(out.numel()) * 2},
+            "roofline": {"bound": "hbm", "achieved": dom["GBps"], "peak": peak, "unit": "GB/s",
+                         "frac": dom["frac"],
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs, copy bandwidth)",
+                         "kernel": dom["kernel"], "launch": dom_kind, "kernel_us": dom["us_per_launch"],
+                         "bytes_per_launch": dom["bytes_per_launch"],
+                         "traffic": recorded_traffic(dom["kernel"].split("<")[0], workload)},
+            "kernels": kernels,
+            "gpu_launches": args.steps * (4 * c["layers"] + 1),
+            "graph_equals_eager": same, "device_status": int(status),
+            "clocks": clk.summary(),
         }
-    if rank == 0 and world == 1 and not args.no_cpu:
-        rows = 8192
-        cpu = cpu_baseline_f16(x.cpu(), w[:rows].cpu(), budget_s=args.cpu_seconds)
-        line["cpu_baseline"] = cpu
+    if world == 1:
+        del model
+        torch.cuda.empty_cache()
+        ws = torch.zeros(lib.b2_workspace_bytes(local), dtype=torch.uint8, device="cuda")
+        l2 = torch.cuda.get_device_properties(local).L2_cache_size
+        extra = {}
+        for key, kind, cfg in (("config1_fp16_lm_head", "f16", dict(CFG1, G=0)),
+                               ("config0_w4", "w4", CFG0)):
+            r = measure_gemm(lib, capi, ws, key, kind, cfg["M"], cfg["K"], cfg["N"], cfg["G"],
+                             200, args.warmup, peak, l2)
+            extra[key] = {k: r[k] for k in ("M", "K", "N", "G", "us", "TBps", "frac", "bytes",
+                                            "l2_rotation_copies")}
+            torch.cuda.empty_cache()
+        line["extra"] = extra
+        if not args.no_cpu:
+            from oracle import cpu_baseline
+
+            cb = cpu_baseline.time_decode_step(CFG4, budget_s=args.cpu_seconds)
+            cb["cpu_model"] = cpu_model()
+            line["cpu_baseline"] = cb
     if line:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -301,8 +535,11 @@ def run_gpu(args):
 
 
 def run_reference(args):
-    """The reference's CPU implementation of the path (oracle port of kernels/bench_skinny.py:44:
-    `x.float() @ w.float().T`), on the same config and metric, all host threads."""
+    """The reference's CPU implementation of the path (oracle port of kernels/check_w4.py:11-21
+    and kernels/bench_skinny.py:44) on the default line's step and metric, all host threads.
+    Each step is a sample (a column sample of every GEMM of one layer and a row sample of the
+    lm_head) scaled to a full config-4 step; the CPU computes the whole step, all ranks' shards.
+    Under torchrun only rank 0 runs."""
     import torch
 
     rank = int(os.environ.get("RANK", "0"))
@@ -310,47 +547,84 @@ def run_reference(args):
         return
     from oracle import cpu_baseline
 
-    M, K, N = CFG1["M"], CFG1["K"], CFG1["N"]
     torch.set_num_threads(os.cpu_count() or 1)
-    g = torch.Generator().manual_seed(1234)
-    x = torch.randn(M, K, generator=g).half()
-    w = (torch.randn(8192, K, generator=g) * 0.02).half()
-    # size the per-step sample so that warm-up + steps stay within about two minutes
-    t0 = time.perf_counter()
-    cpu_baseline.f16_reference(x, w)
-    t_full = time.perf_counter() - t0
-    per_step = 120.0 / (args.steps + args.warmup)
-    rows = int(max(256, min(8192, 8192 * per_step / max(t_full, 1e-6))) // 256 * 256)
-    w = w[:rows].contiguous()
-    step = lambda: cpu_baseline.f16_reference(x, w)  # noqa: E731
+    sample = cpu_baseline.DecodeStepSample(CFG4)
     for _ in range(args.warmup):
-        step()
-    times = []
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        step()
-        times.append(time.perf_counter() - t0)
-    sec = sum(times) / len(times)
-    sample_bytes = f16_bytes(M, K, rows)
-    value = sample_bytes / sec / 1e12
-    desc = (f"{rows} of {N} weight rows per step ({sample_bytes / f16_bytes(M, K, N):.3f} of a "
-            f"config-1 GEMM); torch {torch.__version__} float32 matmul")
+        sample.estimate_step_seconds()
+    est = [sample.estimate_step_seconds() for _ in range(args.steps)]
+    sec = sum(est) / len(est)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": UNIT,
-        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
-        "ms_per_full_gemm": round(sec * 1e3 * N / rows, 1),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f32 (reference computes x.float() @ w.float().T)", "data": "synthetic",
-        "config": {"workload": "config 1: fp16 skinny GEMM, lm_head shape", "M": M, "K": K,
-                   "N": N, "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(value, 6), "unit": UNIT, "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": desc},
-        "e2e": {"value": round(value, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
+        "impl": "reference", "metric": METRIC, "value": round(sec * 1e6, 1), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32 (the reference's torch check computes (q - z) * s and x @ deq; float32 here)",
+        "data": "synthetic",
+        "config": {"workload": "config 4: decode-verify step, 64 W4A16 layers + fp16 lm_head",
+                   "M": CFG4["M"], "tp": world, "layers": CFG4["layers"],
+                   "parallelism": "host cores (the whole step, every rank's shard)"},
+        "cpu_baseline": {"value": round(sec * 1e6, 1), "unit": UNIT,
+                         "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample.describe(), "cpu_model": cpu_model()},
+        "e2e": {"value": round(sec * 1e6, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
+
+def run_config1(args):
+    """BASELINE config 1 alone (the earlier default line): the fp16 lm_head GEMM through the C
+    ABI on device-resident operands, back to back; TB/s of algorithmic bytes."""
+    import torch
+
+    import __graft_entry__ as entry
+
+    rank, world, local = dist_setup(args.gpus)
+    entry.load_package()
+    from mi50_vllm_lab_b200 import capi
+
+    lib = capi.lib()
+    M, K, N = CFG1["M"], CFG1["K"], CFG1["N"]
+    nbytes = f16_bytes(M, K, N)
+    g = torch.Generator(device="cuda").manual_seed(1234 + rank)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    ws = torch.zeros(lib.b2_workspace_bytes(local), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+
+    def step():
+        capi.check(lib.b2_gemm_f16(x.data_ptr(), w.data_ptr(), y.data_ptr(), M, K, N,
+                                   ws.data_ptr(), ws.numel(), sp), "b2_gemm_f16")
+
+    for _ in range(args.warmup):
+        step()
+    with ClockSampler(local) as clk:
+        total_ms = time_steps(step, args.steps, world, stream)
+    ms_step = max_over_ranks(total_ms / args.steps, world)
+    peak, peak_kind = hbm_peak()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "config 1: fp16 skinny GEMM (lm_head shape) HBM throughput", "unit": "TB/s",
+            "value": round(world * nbytes / (ms_step * 1e-3) / 1e12, 4), "n_gpus": world,
+            "us_per_gemm": round(ms_step * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "roofline": {"bound": "hbm", "achieved": round(nbytes / (ms_step * 1e-3) / 1e9, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(nbytes / (ms_step * 1e6) / peak, 4),
+                         "peak_source": peak_kind, "kernel": "gemm_f16_kernel",
+                         "traffic": recorded_traffic("gemm_f16_kernel", "config1")},
+            "clocks": clk.summary()}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# fp16 drafter layers of kernels/bench_skinny.py:34-37, as (N, K) - the reference's own table
+DRAFTER = {"qkv": (3072, 5120), "o": (5120, 2048), "gate_up": (17408, 5120), "down": (5120, 8704),
+           "fc": (5120, 25600), "ctx_kv": (5120, 5120), "kproj": (1280, 5120)}
 
 SWEEP = (
     [("cfg1_lm_head", "f16", 7, 5120, 151936, 0), ("cfg0", "w4", 7, 4096, 4096, 128)]
@@ -358,7 +632,9 @@ SWEEP = (
        for nm, (K, N) in {"qkv": (5120, 8192), "o_proj": (6144, 5120), "gate_up": (5120, 34816),
                           "down": (17408, 5120)}.items()]
     + [(f"cfg3_down_TP{P}", "w4", 8, 17408 // P, 5120, 128) for P in (2, 4, 8)]
-    + [(f"drafter_fc_M{M}", "f16", M, 25600, 5120, 0) for M in (1, 8)]
+    + [(f"cfg4_TP8_{nm}", "w4", 8, K, N, 128) for nm, (K, N) in layer_shapes(8).items()]
+    + [(f"drafter_{nm}_M{M}", "f16", M, K, N, 0) for M in (1, 7, 8)
+       for nm, (N, K) in DRAFTER.items()]
     + [("check_w4_G32", "w4", 8, 5120, 1024, 32)]
 )
 # Extra cases for --profile only: the lm_head kernel on a 335 MB slice (above L2, small enough
@@ -367,9 +643,8 @@ PROFILE_ONLY = [("cfg1_lm_head_N32768", "f16", 7, 5120, 32768, 0)]
 
 
 def run_sweep(args):
-    """Every BASELINE config on one GPU. Launches are captured in a CUDA graph that rotates over
-    enough weight copies to exceed 3x L2 (so every launch reads HBM), and timed by replaying the
-    graph: the time per launch excludes host launch overhead, as in a captured decode step."""
+    """Every single-GEMM BASELINE config (and the drafter shapes of kernels/bench_skinny.py:34-38)
+    on one GPU, timed by graph replay over > 3x L2 of weight copies (see measure_gemm)."""
     import torch
 
     import __graft_entry__ as entry
@@ -387,70 +662,13 @@ def run_sweep(args):
         capi.check(lib.b2_set_tuning(k, v), "b2_set_tuning")
     peak, _ = hbm_peak()
     l2 = torch.cuda.get_device_properties(0).L2_cache_size
-
-    def measure(name, kind, M, K, N, G):
-        wbytes = K * N // 2 if kind == "w4" else 2 * N * K
-        nb = w4_bytes(M, K, N, G) if kind == "w4" else f16_bytes(M, K, N)
-        copies = max(1, int(3 * l2 // wbytes) + 1)
-        g = torch.Generator(device="cuda").manual_seed(M * K + N)
-        x = torch.randn(M, K, device="cuda", generator=g).half()
-        y = torch.empty(M, N, dtype=torch.float16, device="cuda")
-        calls = []
-        for _ in range(copies):
-            if kind == "w4":
-                qw = torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32, generator=g)
-                qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda", dtype=torch.int32, generator=g)
-                sc = (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half()
-                calls.append((qw, qz, sc))
-            else:
-                calls.append((torch.randn(N, K, device="cuda", generator=g) * 0.02).half(),)
-
-        def launch(t, sp):
-            if kind == "w4":
-                qw, qz, sc = t
-                rc = lib.b2_w4_gemm(x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(),
-                                    y.data_ptr(), M, K, N, G, ws.data_ptr(), ws.numel(), sp)
-            else:
-                rc = lib.b2_gemm_f16(x.data_ptr(), t[0].data_ptr(), y.data_ptr(), M, K, N,
-                                     ws.data_ptr(), ws.numel(), sp)
-            capi.check(rc, name)
-
-        reps = max(copies, min(64, 20 * copies))
-        reps = (reps // copies) * copies
-        sp0 = torch.cuda.current_stream().cuda_stream
-        for t in calls:
-            launch(t, sp0)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        s = torch.cuda.Stream()
-        s.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(graph, stream=s):
-                for i in range(reps):
-                    launch(calls[i % copies], s.cuda_stream)
-        torch.cuda.current_stream().wait_stream(s)
-        for _ in range(args.warmup):
-            graph.replay()
-        torch.cuda.synchronize()
-        st = torch.cuda.current_stream()
-        times = []
-        for _ in range(max(3, args.steps // reps)):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            graph.replay()
-            e1.record(st)
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1) * 1e3 / reps)
-        us = statistics.median(times)
-        del graph
-        return {"workload": name, "kind": kind, "M": M, "K": K, "N": N, "G": G, "us": round(us, 2),
-                "TBps": round(nb / us / 1e6, 3), "frac": round(nb / us / 1e3 / peak, 3),
-                "bytes": nb, "l2_rotation_copies": copies, "launches_per_graph": reps}
-
     for w in SWEEP:
         if args.only and not any(o in w[0] for o in args.only.split(",")):
             continue
-        print(json.dumps(measure(*w)), flush=True)
+        r = measure_gemm(lib, capi, ws, *w, args.steps, args.warmup, peak, l2)
+        if w[1] == "w4":
+            r["plan"] = capi.w4_plan(w[2], w[3], w[4], w[5])
+        print(json.dumps(r), flush=True)
         torch.cuda.empty_cache()
 
 
@@ -487,130 +705,6 @@ def run_profile(args):
     torch.cuda.synchronize()
     print(json.dumps({"profiled": name, "launches": args.warmup + args.steps}))
 
-
-# the decode-verify step of a 64-layer W4A16 model at M = 8 (speculative k = 7),
-# tensor parallel over the ranks: qkv and gate_up column-parallel, o_proj and down_proj
-# row-parallel with the NVLink all-reduce fused into their epilogues, then the fp16 lm_head
-# (column-parallel, 151936 / P rows per rank), all captured in one CUDA graph.
-CFG4 = dict(layers=64, M=8, hidden=5120, qkv=8192, o_in=6144, inter=17408, vocab=151936, G=128)
-
-
-def decode_step_bytes(P: int) -> int:
-    c = CFG4
-    per_layer = (w4_bytes(c["M"], c["hidden"], c["qkv"] // P, c["G"])
-                 + w4_bytes(c["M"], c["o_in"] // P, c["hidden"], c["G"])
-                 + w4_bytes(c["M"], c["hidden"], 2 * c["inter"] // P, c["G"])
-                 + w4_bytes(c["M"], c["inter"] // P, c["hidden"], c["G"]))
-    return c["layers"] * per_layer + f16_bytes(c["M"], c["hidden"], c["vocab"] // P)
-
-
-def run_decode_step(args):
-    """Config 4 on N GPUs (TP = N): one graph replay per step, timed as the max over ranks."""
-    import torch
-
-    import __graft_entry__ as entry
-
-    rank, world, local = dist_setup(args.gpus)
-    pkg = entry.load_package()
-    from mi50_vllm_lab_b200 import vllm_shim
-
-    ops = pkg.ops()
-    c = CFG4
-    M, H, G, P = c["M"], c["hidden"], c["G"], world
-    ar = None
-    if P > 1:
-        import datetime
-
-        import torch.distributed as dist
-
-        cpu = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=120))
-        # 8 bytes per output element: room for the low-latency (value + generation) exchange
-        ar = vllm_shim.NvlinkAllReduce(cpu, rank, list(range(P)), slot_bytes=M * H * 8)
-    g = torch.Generator(device="cuda").manual_seed(4000 + rank)
-
-    def w4(K, N):
-        return (torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32,
-                              generator=g),
-                torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda",
-                              dtype=torch.int32, generator=g),
-                (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half())
-
-    layers = [dict(qkv=w4(H, c["qkv"] // P), o=w4(c["o_in"] // P, H),
-                   gu=w4(H, 2 * c["inter"] // P), down=w4(c["inter"] // P, H))
-              for _ in range(c["layers"])]
-    lm = (torch.randn(c["vocab"] // P, H, device="cuda", generator=g) * 0.02).half()
-    x0 = torch.randn(M, H, device="cuda", generator=g).half()
-    # attention output and activated MLP input of this rank's shard (synthetic, fixed)
-    a_o = (torch.randn(M, c["o_in"] // P, device="cuda", generator=g) * 0.05).half()
-    a_d = (torch.randn(M, c["inter"] // P, device="cuda", generator=g) * 0.05).half()
-
-    def row_parallel(a, w):
-        return ar.w4_gemm_all_reduce(a, *w) if ar else ops.w4gemm(a, *w, 0, 0)
-
-    def step():
-        h = x0
-        for L in layers:
-            ops.w4gemm(h, *L["qkv"], 0, 0)
-            h = row_parallel(a_o, L["o"])
-            ops.w4gemm(h, *L["gu"], 0, 0)
-            h = row_parallel(a_d, L["down"])
-        return ops.gemm(h, lm, 0)
-
-    eager = step()
-    torch.cuda.synchronize()
-    s = torch.cuda.Stream()
-    s.wait_stream(torch.cuda.current_stream())
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(s):
-        with torch.cuda.graph(graph, stream=s):
-            out = step()
-    torch.cuda.current_stream().wait_stream(s)
-    for _ in range(args.warmup):
-        graph.replay()
-    torch.cuda.synchronize()
-    same = bool(torch.equal(out, eager))
-    st = torch.cuda.current_stream()
-    align = torch.zeros(1, device="cuda")
-    times = []
-    with ClockSampler(local) as clk:
-        for _ in range(args.steps):
-            if P > 1:
-                import torch.distributed as dist
-
-                dist.all_reduce(align)  # line the ranks up on the device, not on the host
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(st)
-            graph.replay()
-            e1.record(st)
-            e1.synchronize()
-            times.append(e0.elapsed_time(e1) * 1e3)
-    us = max_over_ranks(statistics.median(times), world)
-    status = ar.status() if ar else ops.workspace_status(False)
-    nbytes = decode_step_bytes(P)
-    peak, peak_kind = hbm_peak()
-    if rank == 0:
-        kernels = c["layers"] * 4 + 1
-        print(json.dumps({
-            "metric": "config 4: decode-verify step (64 W4A16 layers + fp16 lm_head, M=8), us per step",
-            "value": round(us, 1), "unit": "us", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": False, "scaling": "strong",
-            "dtype": "W4A16 / f16 (fp32 accumulate)", "data": "synthetic (seeded random weights)",
-            "config": {"workload": "config 4", "tp": P, "layers": c["layers"], "M": M,
-                       "kernels_per_step": kernels, "fused_allreduces_per_step": 2 * c["layers"] if P > 1 else 0,
-                       "graph": "one CUDA graph per step (programmatic dependent launch between GEMMs)",
-                       "per_rank_bytes_per_step": nbytes},
-            "per_rank_TBps": round(nbytes / us / 1e6, 3),
-            "roofline": {"bound": "hbm", "achieved": round(nbytes / us / 1e3, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(nbytes / us / 1e3 / peak, 4),
-                         "peak_source": peak_kind},
-            "graph_equals_eager": same, "device_status": status, "clocks": clk.summary()}),
-            flush=True)
-    del graph
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-        dist.destroy_process_group()
 
 
 def run_norm_epilogue(args):
@@ -721,15 +815,17 @@ def run_norm_epilogue(args):
             torch.cuda.empty_cache()
 
 
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--sweep", action="store_true")
-    ap.add_argument("--decode-step", action="store_true",
-                    help="config 4: the 64-layer decode-verify step in one CUDA graph, TP = --gpus")
+    ap.add_argument("--config1", action="store_true",
+                    help="config 1 alone: the fp16 lm_head GEMM back to back (TB/s)")
     ap.add_argument("--only", default="", help="with --sweep: workloads whose name contains one of these comma-separated "
                          "strings; with --profile: the first workload whose name contains it")
     ap.add_argument("--profile", action="store_true", help="eager launches of one --only workload (for ncu)")
@@ -750,8 +846,8 @@ def main():
         run_profile(args)
     elif args.sweep:
         run_sweep(args)
-    elif args.decode_step:
-        run_decode_step(args)
+    elif args.config1:
+        run_config1(args)
     elif args.norm_epilogue:
         run_norm_epilogue(args)
     else:

@@ -127,10 +127,16 @@ int b2_w4_gemm(const void* a, const void* qw, const void* qz, const void* sc, vo
  * workspace alive between calls. This entry point calls no cudaMalloc, cudaFree or other
  * allocating routine.
  *   - Limit: N <= 524288 (4096 output tiles of 128 columns); larger N is rejected with
- *     B2_ERR_INVALID_ARG. The split-K grid is capped at 256 CTAs.
- *   - The first call on a device looks up the array's device address and zero-fills it, with a
- *     synchronous cudaMemset; make that first call before any CUDA graph capture.
- *   - Every call clears the array's counters on `stream` (cudaMemsetAsync) before its kernel.
+ *     B2_ERR_INVALID_ARG. When the shape's plan is stream-K its grid is capped at 256 CTAs (the
+ *     array's partial slots); when the plan is the thread-block-cluster kernel, which reduces
+ *     through distributed shared memory and uses none of the array, the call launches exactly as
+ *     b2_w4_gemm does.
+ *   - The first call in a CUDA context (per device; for runtime-API callers the device's primary
+ *     context) looks up the array's device address with cudaGetSymbolAddress. Make that first
+ *     call before any CUDA graph capture: inside a capture it fails with B2_ERR_STATE. A call from
+ *     another context, or after cudaDeviceReset, looks the address up again.
+ *   - A stream-K call clears the array's status word and the tile counters it uses on `stream`
+ *     (cudaMemsetAsync) before its kernel, so it never depends on what an earlier call left.
  *   - All calls on a device share the one array: calls that can overlap on the GPU (different
  *     streams, or graphs replayed concurrently) race and give wrong results. Issue them in order.
  *   - A device-side wait that gives up is recorded only in the array, which no entry point
@@ -138,6 +144,10 @@ int b2_w4_gemm(const void* a, const void* qw, const void* qz, const void* sc, vo
  * ---------------------------------------------------------------------------------------- */
 int b2_w4_gemm_noalloc(const void* a, const void* qw, const void* qz, const void* sc, void* y,
                        int M, int K, int N, int group_size, void* stream);
+/* Device address and size of that fixed array on the current device (the address
+ * b2_w4_gemm_noalloc passes to its kernels), for diagnostics and tests. Same set-up rule as the
+ * first b2_w4_gemm_noalloc call: not inside a stream capture. No counterpart in the reference. */
+int b2_w4_noalloc_scratch(void** device_ptr, size_t* bytes);
 
 /* ------------------------------------------------------------------------------------------
  * Host-side rendezvous registry (POSIX shared memory, no GPU needed)
@@ -234,6 +244,14 @@ int b2_nvar_destroy(b2_nvar* ar);
 #define B2_TUNE_W4_CLUSTER 5      /* cluster path: CTAs per cluster (0 = chosen per shape)      */
 int b2_set_tuning(int key, int value);
 int b2_get_tuning(int key);
+
+/* The split-K plan that b2_w4_gemm (fused == 0) or b2_w4_gemm_allreduce with the 64-bit exchange
+ * (fused != 0) would launch for this shape on the current device, under the current tuning:
+ * *path = 1 (stream-K, kernel w4_kernel) or 2 (thread-block clusters, kernel w4c_kernel),
+ * *cluster = CTAs per cluster (0 for stream-K), *ctas = CTAs of the grid. For benchmarks and
+ * profiles, which name the kernel they time. No counterpart in the reference, whose grid is fixed
+ * by its kw and waves arguments (kernels/w4.cu:489-500). */
+int b2_w4_plan(int M, int K, int N, int group_size, int fused, int* path, int* cluster, int* ctas);
 
 #ifdef __cplusplus
 }

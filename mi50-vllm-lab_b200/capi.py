@@ -40,6 +40,7 @@ _SIGS = {
     "b2_gemm_f16": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     "b2_w4_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "b2_w4_gemm_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "b2_w4_noalloc_scratch": (_i, [C.POINTER(_vp), C.POINTER(_sz)]),
     "b2_registry_open": (_i, [C.c_char_p, _i, _i, C.POINTER(_vp)]),
     "b2_registry_put": (_i, [_vp, _i, _vp]),
     "b2_registry_get": (_i, [_vp, _i, _vp]),
@@ -61,6 +62,7 @@ _SIGS = {
     "b2_nvar_destroy": (_i, [_vp]),
     "b2_set_tuning": (_i, [_i, _i]),
     "b2_get_tuning": (_i, [_i]),
+    "b2_w4_plan": (_i, [_i, _i, _i, _i, _i, C.POINTER(_i), C.POINTER(_i), C.POINTER(_i)]),
 }
 
 _lib = None
@@ -100,3 +102,13 @@ class B2Error(RuntimeError):
 def check(status: int, where: str = "b2") -> None:
     if status != B2_OK:
         raise B2Error(status, where)
+
+
+def w4_plan(M: int, K: int, N: int, G: int, fused: bool = False) -> dict:
+    """The split-K plan the W4 entry points would launch (b2_w4_plan): the kernel's name, the
+    path (1 stream-K, 2 clusters), CTAs per cluster and the grid size."""
+    path, cs, ctas = C.c_int(), C.c_int(), C.c_int()
+    check(lib().b2_w4_plan(M, K, N, G, 1 if fused else 0, C.byref(path), C.byref(cs),
+                           C.byref(ctas)), "b2_w4_plan")
+    kernel = "w4c_kernel" if path.value == 2 else "w4_kernel"
+    return {"kernel": kernel, "path": path.value, "cluster": cs.value, "ctas": ctas.value}

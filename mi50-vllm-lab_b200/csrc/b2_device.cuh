@@ -61,14 +61,30 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with an explicit suspend-time hint: a thread whose phase has not completed sleeps in
+// hardware for up to `hint_ns` (waking early when the phase completes) instead of returning at
+// once, so a waiting warp issues almost nothing while it waits.
+__device__ __forceinline__ bool mbar_test_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for phase `parity` of `bar` to complete. Gives up after kPipeWaitNs, or at once when
 // another warp of the CTA already gave up (*abort != 0); then sets *abort and returns false.
+// After the first test each poll suspends the thread (up to 20 us) until the phase completes.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
   if (mbar_test(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (unsigned int it = 1; it < kMaxSpin; ++it) {
-    if (mbar_test(bar, parity)) return true;
-    if ((it & 63u) == 0) {
+    if (mbar_test_hint(bar, parity, 20000u)) return true;
+    if ((it & 7u) == 0) {
       if (*abort) return false;
       if (globaltimer_ns() - t0 > kPipeWaitNs) break;
     }
@@ -144,6 +160,15 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
                : "memory");
   return v;
 }
+// The same at addr + 1024 (immediate offset: no address arithmetic).
+__device__ __forceinline__ uint4 lds128_1k(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4+1024];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
 __device__ __forceinline__ uint4 ldg_nc128(const void* p) {
   uint4 v;
   asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
@@ -193,6 +218,17 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a
       "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// The same with C = 0: the first mma of an accumulation needs no zeroed registers.
+__device__ __forceinline__ void mma_16816_first(float (&d)[4], uint32_t a0, uint32_t a1,
+                                                uint32_t a2, uint32_t a3, uint32_t b0,
+                                                uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %11, %12, %13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(0.f), "f"(0.f), "f"(0.f),
+        "f"(0.f));
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -127,6 +127,169 @@ __device__ __forceinline__ void dequant_word(uint32_t q, uint32_t zlo, uint32_t 
   d[3] = hadd2_u(lop_and_or(q8, 0x00F000F0u, kHi), zhi);
 }
 
+// The same 8 nibbles without the zero point: (1024 + q) for the nibbles at bits 0..3 of a half
+// (k = 0,1,4,5 of the word) and (64 + q) for those at bits 4..7 (k = 2,3,6,7). One shift and four
+// lop3 per word; the offsets and the zero point are removed once per group (GroupFix).
+__device__ __forceinline__ void dequant_word_off(uint32_t q, uint32_t (&d)[4]) {
+  constexpr uint32_t kLo = 0x64006400u;  // 1024.0 | 1024.0
+  constexpr uint32_t kHi = 0x54005400u;  // 64.0 | 64.0
+  const uint32_t q8 = q >> 8;
+  d[0] = lop_and_or(q, 0x000F000Fu, kLo);
+  d[1] = lop_and_or(q, 0x00F000F0u, kHi);
+  d[2] = lop_and_or(q8, 0x000F000Fu, kLo);
+  d[3] = lop_and_or(q8, 0x00F000F0u, kHi);
+}
+
+// Per-lane shared-memory geometry of the consumer warps. Lane (g = lane/4, t = lane%4) of warp w
+// owns columns colw .. colw+3 of a unit (colw = w*32 + 4*ch, ch = the lane's 16-byte chunk of a
+// 128-byte word row, permuted so the swizzled loads are conflict-free). For 32-k step q it reads
+// word row 4q+t of its chunk and the matching 16 bytes of activations of row g (chunk 4q+t of
+// the stage's two 64-k boxes). Under the 128-byte swizzle, steps 2 and 3 sit exactly 1024 bytes
+// after steps 0 and 1 in both blocks, so two base offsets per block cover the four steps.
+struct LaneGeo {
+  int g, t, ch, colw;
+  uint32_t xa, xb;  // activations of steps 0 / 1 inside a stage's x block (+1024: steps 2 / 3)
+  uint32_t wa, wb;  // weight chunks of steps 0 / 1 inside the warp's qw box (+1024: steps 2 / 3)
+  uint32_t one, zero;  // 1.0|1.0 and 0 in registers (a constant A operand kept live)
+  __device__ __forceinline__ LaneGeo(int warp, int lane, int M) {
+    g = lane >> 2;
+    t = lane & 3;
+    ch = ((g & 1) << 2) | (g >> 1);
+    colw = warp * 32 + ch * 4;
+    xa = (uint32_t)(g * 128 + ((t ^ g) << 4));
+    xb = (uint32_t)(g * 128 + ((t ^ g ^ 4) << 4));
+    wa = (uint32_t)(t * 128 + ((ch ^ t) << 4));
+    wb = (uint32_t)((4 + t) * 128 + ((ch ^ t ^ 4) << 4));
+    // M <= 8, so M >> 8 is 0; taken from a kernel argument, the compiler keeps these values in
+    // registers instead of rebuilding the constant operand at every use
+    zero = (uint32_t)M >> 8;
+    one = 0x3C003C00u | zero;
+  }
+};
+
+// Consume one unit (128 columns x 128 k) from a stage: acc[T][i] += this unit's contribution,
+// scaled per quantization group, for the lane's columns colw + 2T + (i >> 1) and rows 2t + (i & 1).
+// x_base / qw_base: shared addresses of the stage's activations and of this warp's qw box;
+// sc_row / qz_row: the stage's scale rows [RG][128] fp16 and zero rows [RG][16] int32.
+//
+// G >= 128 (one group per unit) uses the offset form: the tensor cores multiply the activations
+// by (off_k + q) straight from dequant_word_off (off_k = 1024 for the nibbles at bits 0..3 of a
+// half, 64 for bits 4..7), and two more mma per 32 k against a constant A (ones on the 1024
+// slots in rows 0..7, ones on the 64 slots in rows 8..15) give every lane XL[m] and XH[m], the
+// row sums of the activations on the two kinds of slot. Per group, for column n and row m:
+//   sum_k (q - z) x  =  raw - 1024 XL - 64 XH - z (XL + XH),
+// which is multiplied by the group's scale in fp32. Per 8-weight word that is one shift and four
+// lop3 (the exact form below needs four add.f16x2 more), at the price of carrying the offsets
+// through the fp32 accumulation (rounding error ~1e-3 of a group sum of ~1e4, far inside the
+// fp16 output rounding).
+// G = 32 / 64 use the exact form: A = (q - z) exactly in fp16 (dequant_word), scale per group.
+template <int GP>
+__device__ __forceinline__ void consume_unit(const LaneGeo& L, uint32_t x_base, uint32_t qw_base,
+                                             const __half* sc_rows, const uint32_t* qz_rows,
+                                             float (&acc)[2][4]) {
+  constexpr int RG = 4 / GP;
+  uint4 xv[4], wv[4];
+  const uint32_t xa = x_base + L.xa, xb = x_base + L.xb;
+  const uint32_t wa = qw_base + L.wa, wb = qw_base + L.wb;
+  xv[0] = lds128(xa);
+  xv[1] = lds128(xb);
+  xv[2] = lds128_1k(xa);
+  xv[3] = lds128_1k(xb);
+  wv[0] = lds128(wa);
+  wv[1] = lds128(wb);
+  wv[2] = lds128_1k(wa);
+  wv[3] = lds128_1k(wb);
+  if constexpr (GP == 4) {
+    float raw[2][4], xs[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 w = wv[q];
+      uint32_t d0[4], d1[4], d2[4], d3[4];
+      dequant_word_off(w.x, d0);
+      dequant_word_off(w.y, d1);
+      dequant_word_off(w.z, d2);
+      dequant_word_off(w.w, d3);
+      // n-tile 0: A rows g / g+8 = columns colw / colw+1; n-tile 1: colw+2 / colw+3. In every
+      // mma the A registers a0/a1 hold the 1024-offset pairs and a2/a3 the 64-offset pairs.
+      if (q == 0) {
+        mma_16816_first(raw[0], d0[0], d1[0], d0[1], d1[1], xv[q].x, xv[q].y);
+        mma_16816_first(raw[1], d2[0], d3[0], d2[1], d3[1], xv[q].x, xv[q].y);
+        mma_16816_first(xs, L.one, L.zero, L.zero, L.one, xv[q].x, xv[q].y);
+      } else {
+        mma_16816(raw[0], d0[0], d1[0], d0[1], d1[1], xv[q].x, xv[q].y);
+        mma_16816(raw[1], d2[0], d3[0], d2[1], d3[1], xv[q].x, xv[q].y);
+        mma_16816(xs, L.one, L.zero, L.zero, L.one, xv[q].x, xv[q].y);
+      }
+      mma_16816(raw[0], d0[2], d1[2], d0[3], d1[3], xv[q].z, xv[q].w);
+      mma_16816(raw[1], d2[2], d3[2], d2[3], d3[3], xv[q].z, xv[q].w);
+      mma_16816(xs, L.one, L.zero, L.zero, L.one, xv[q].z, xv[q].w);
+    }
+    // xs: XL[2t], XL[2t+1] (rows 0..7 of D), XH[2t], XH[2t+1] (rows 8..15)
+    const float x0[2] = {xs[0] + xs[2], xs[1] + xs[3]};
+    const float c1[2] = {fmaf(1024.f, xs[0], 64.f * xs[2]), fmaf(1024.f, xs[1], 64.f * xs[3])};
+    const uint32_t zw = qz_rows[L.colw >> 3] >> ((L.colw & 7) * 4);
+    const uint2 sv = *reinterpret_cast<const uint2*>(sc_rows + L.colw);
+    const __half2 s01 = *reinterpret_cast<const __half2*>(&sv.x);
+    const __half2 s23 = *reinterpret_cast<const __half2*>(&sv.y);
+    const float s[4] = {__low2float(s01), __high2float(s01), __low2float(s23), __high2float(s23)};
+#pragma unroll
+    for (int T = 0; T < 2; ++T)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = 2 * T + (i >> 1), j = i & 1;
+        const float z = (float)((zw >> (4 * c)) & 0xFu);
+        acc[T][i] = fmaf(s[c], raw[T][i] - fmaf(z, x0[j], c1[j]), acc[T][i]);
+      }
+  } else {
+    // zero points and scales of the lane's 4 columns for each group row of the unit
+    uint32_t zlo[RG][4], zhi[RG][4];
+    float scl[RG][4];
+#pragma unroll
+    for (int r = 0; r < RG; ++r) {
+      const uint32_t zw = qz_rows[r * (kTileN / 8) + (L.colw >> 3)] >> ((L.colw & 7) * 4);
+      const uint2 sv = *reinterpret_cast<const uint2*>(sc_rows + r * kTileN + L.colw);
+      const __half2 s01 = *reinterpret_cast<const __half2*>(&sv.x);
+      const __half2 s23 = *reinterpret_cast<const __half2*>(&sv.y);
+      scl[r][0] = __low2float(s01);
+      scl[r][1] = __high2float(s01);
+      scl[r][2] = __low2float(s23);
+      scl[r][3] = __high2float(s23);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t z = (zw >> (4 * i)) & 0xFu;
+        zlo[r][i] = (0xE400u + z) * 0x00010001u;         // -(1024 + z)
+        zhi[r][i] = (0xD400u + (z << 4)) * 0x00010001u;  // -(64 + z)
+      }
+    }
+    float accg[2][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) accg[0][i] = accg[1][i] = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // 32-k step q: word rows 4q..4q+3, lane t takes row 4q+t
+      const uint4 w = wv[q];
+      const int r = (RG == 1) ? 0 : (q / GP);
+      uint32_t d0[4], d1[4], d2[4], d3[4];
+      dequant_word(w.x, zlo[r][0], zhi[r][0], d0);
+      dequant_word(w.y, zlo[r][1], zhi[r][1], d1);
+      dequant_word(w.z, zlo[r][2], zhi[r][2], d2);
+      dequant_word(w.w, zlo[r][3], zhi[r][3], d3);
+      mma_16816(accg[0], d0[0], d1[0], d0[1], d1[1], xv[q].x, xv[q].y);
+      mma_16816(accg[0], d0[2], d1[2], d0[3], d1[3], xv[q].z, xv[q].w);
+      mma_16816(accg[1], d2[0], d3[0], d2[1], d3[1], xv[q].x, xv[q].y);
+      mma_16816(accg[1], d2[2], d3[2], d2[3], d3[3], xv[q].z, xv[q].w);
+      if ((q + 1) % GP == 0) {
+#pragma unroll
+        for (int T = 0; T < 2; ++T)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            acc[T][i] = fmaf(scl[r][2 * T + (i >> 1)], accg[T][i], acc[T][i]);
+            accg[T][i] = 0.f;
+          }
+      }
+    }
+  }
+}
+
 // Lane output layout of a 128-column tile: lane (g, t) of warp w owns columns
 // w*32 + 4*ch(g) .. +3 for rows m = 2t (v[0]) and m = 2t+1 (v[1]).
 __device__ __forceinline__ void store_y(const W4Args& p, int tile, int colw, int t,
@@ -325,7 +488,6 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
               const __grid_constant__ CUtensorMap tm_qz, const __grid_constant__ CUtensorMap tm_x,
               const W4Args p, const ArView ar) {
   using C = Cfg<GP>;
-  constexpr int RG = C::RG;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -427,16 +589,16 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
   grid_dep_wait();
   if (FUSED && threadIdx.x == 0) *s_gen = ar_begin(ar);
   named_bar_sync(1, kWarps * 32);
-  const int g = lane >> 2, t = lane & 3;
-  const int ch = ((g & 1) << 2) | (g >> 1);  // 16-byte chunk (4 columns) of the 128-byte row
-  const int colw = warp * 32 + ch * 4;       // lane's first column inside the tile
+  const LaneGeo L(warp, lane, p.M);
+  const int t = L.t, colw = L.colw;
   const uint32_t e = FUSED ? *s_gen : 0u;
+  const uint32_t x_base0 = smem_u32(s_x), qw_base0 = smem_u32(s_qw + warp * kQwBox);
 
-  float acc[2][4], accg[2][4];
+  float acc[2][4];
 #pragma unroll
   for (int T = 0; T < 2; ++T)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[T][i] = accg[T][i] = 0.f;
+    for (int i = 0; i < 4; ++i) acc[T][i] = 0.f;
 
   int st = 0;
   uint32_t ph = 0;
@@ -447,63 +609,9 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
     // The lanes poll the barrier one by one, so the warp may be diverged here;
     // mma.sync.aligned needs all 32 lanes converged.
     __syncwarp();
-
-    // activations: lane (g, t) takes chunk 4q + t of row g (box q / 2), the k of its A chunk
-    const uint32_t xb = smem_u32(s_x + st * C::kXBytes) + g * 128;
-    uint4 xv[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) xv[q] = lds128(xb + (q >> 1) * 1024 + ((((4 * q + t) & 7) ^ g) << 4));
-
-    // zero points and scales of the lane's 4 columns for each group row of the unit
-    uint32_t zlo[RG][4], zhi[RG][4];
-    float scl[RG][4];
-#pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      const uint32_t* qz_row =
-          reinterpret_cast<const uint32_t*>(s_qz + st * C::kQzStride) + r * (kTileN / 8);
-      const __half* sc_row = reinterpret_cast<const __half*>(s_sc + st * C::kScStride) + r * kTileN;
-      const uint32_t zw = qz_row[colw >> 3] >> ((colw & 7) * 4);
-      const uint2 sv = *reinterpret_cast<const uint2*>(sc_row + colw);
-      const __half2 s01 = *reinterpret_cast<const __half2*>(&sv.x);
-      const __half2 s23 = *reinterpret_cast<const __half2*>(&sv.y);
-      scl[r][0] = __low2float(s01);
-      scl[r][1] = __high2float(s01);
-      scl[r][2] = __low2float(s23);
-      scl[r][3] = __high2float(s23);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint32_t z = (zw >> (4 * i)) & 0xFu;
-        zlo[r][i] = (0xE400u + z) * 0x00010001u;         // -(1024 + z)
-        zhi[r][i] = (0xD400u + (z << 4)) * 0x00010001u;  // -(64 + z)
-      }
-    }
-
-    const uint32_t qb = smem_u32(s_qw + st * kQwStage + warp * kQwBox);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {  // 32-k pair q: word rows 4q..4q+3, lane t takes row 4q+t
-      const int row = 4 * q + t;
-      const uint4 w = lds128(qb + row * 128 + ((ch ^ (row & 7)) << 4));
-      const int r = (RG == 1) ? 0 : (q / GP);
-      uint32_t d0[4], d1[4], d2[4], d3[4];
-      dequant_word(w.x, zlo[r][0], zhi[r][0], d0);
-      dequant_word(w.y, zlo[r][1], zhi[r][1], d1);
-      dequant_word(w.z, zlo[r][2], zhi[r][2], d2);
-      dequant_word(w.w, zlo[r][3], zhi[r][3], d3);
-      // n-tile 0: A rows g / g+8 = columns colw / colw+1; n-tile 1: colw+2 / colw+3
-      mma_16816(accg[0], d0[0], d1[0], d0[1], d1[1], xv[q].x, xv[q].y);
-      mma_16816(accg[0], d0[2], d1[2], d0[3], d1[3], xv[q].z, xv[q].w);
-      mma_16816(accg[1], d2[0], d3[0], d2[1], d3[1], xv[q].x, xv[q].y);
-      mma_16816(accg[1], d2[2], d3[2], d2[3], d3[3], xv[q].z, xv[q].w);
-      if ((q + 1) % GP == 0) {
-#pragma unroll
-        for (int T = 0; T < 2; ++T)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            acc[T][i] = fmaf(scl[r][2 * T + (i >> 1)], accg[T][i], acc[T][i]);
-            accg[T][i] = 0.f;
-          }
-      }
-    }
+    consume_unit<GP>(L, x_base0 + st * C::kXBytes, qw_base0 + st * kQwStage,
+                     reinterpret_cast<const __half*>(s_sc + st * C::kScStride),
+                     reinterpret_cast<const uint32_t*>(s_qz + st * C::kQzStride), acc);
     fence_proxy_async_smem();  // this lane's reads of the stage precede its next TMA fill
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
@@ -720,7 +828,6 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
                const __grid_constant__ CUtensorMap tm_qz, const __grid_constant__ CUtensorMap tm_x,
                const W4Args p, const ArView ar) {
   using C = CfgC<GP>;
-  constexpr int RG = C::RG;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -832,20 +939,20 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
   grid_dep_wait();
   if (FUSED && threadIdx.x == 0) *s_gen = ar_begin(ar);
   named_bar_sync(1, kWarps * 32);
-  const int g = lane >> 2, t = lane & 3;
-  const int ch = ((g & 1) << 2) | (g >> 1);
-  const int colw = warp * 32 + ch * 4;
+  const LaneGeo L(warp, lane, p.M);
+  const int t = L.t, colw = L.colw;
   const uint32_t e = FUSED ? *s_gen : 0u;
   const int tid = threadIdx.x;
   // column slice of every tile that this CTA reduces and writes
   const int c0 = kTileN * crank / CS, c1 = kTileN * (crank + 1) / CS, W = c1 - c0;
   const uint32_t red_addr = smem_u32(s_red);
+  const uint32_t x_base0 = smem_u32(s_x), qw_base0 = smem_u32(s_qw + warp * kQwBox);
 
-  float acc[2][4], accg[2][4];
+  float acc[2][4];
 #pragma unroll
   for (int T = 0; T < 2; ++T)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[T][i] = accg[T][i] = 0.f;
+    for (int i = 0; i < 4; ++i) acc[T][i] = 0.f;
 
   int st = 0;
   uint32_t ph = 0;
@@ -855,58 +962,9 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
     for (int ku = k0; ku < k1; ++ku) {
       if (ok) ok = mbar_wait(&full[st], ph, s_abort);
       __syncwarp();
-      const uint32_t xb = smem_u32(s_x + st * C::kXBytes) + g * 128;
-      uint4 xv[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        xv[q] = lds128(xb + (q >> 1) * 1024 + ((((4 * q + t) & 7) ^ g) << 4));
-      uint32_t zlo[RG][4], zhi[RG][4];
-      float scl[RG][4];
-#pragma unroll
-      for (int r = 0; r < RG; ++r) {
-        const uint32_t* qz_row =
-            reinterpret_cast<const uint32_t*>(s_qz + st * C::kQzStride) + r * (kTileN / 8);
-        const __half* sc_row = reinterpret_cast<const __half*>(s_sc + st * C::kScStride) + r * kTileN;
-        const uint32_t zw = qz_row[colw >> 3] >> ((colw & 7) * 4);
-        const uint2 sv = *reinterpret_cast<const uint2*>(sc_row + colw);
-        const __half2 s01 = *reinterpret_cast<const __half2*>(&sv.x);
-        const __half2 s23 = *reinterpret_cast<const __half2*>(&sv.y);
-        scl[r][0] = __low2float(s01);
-        scl[r][1] = __high2float(s01);
-        scl[r][2] = __low2float(s23);
-        scl[r][3] = __high2float(s23);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint32_t z = (zw >> (4 * i)) & 0xFu;
-          zlo[r][i] = (0xE400u + z) * 0x00010001u;
-          zhi[r][i] = (0xD400u + (z << 4)) * 0x00010001u;
-        }
-      }
-      const uint32_t qb = smem_u32(s_qw + st * kQwStage + warp * kQwBox);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int row = 4 * q + t;
-        const uint4 w = lds128(qb + row * 128 + ((ch ^ (row & 7)) << 4));
-        const int r = (RG == 1) ? 0 : (q / GP);
-        uint32_t d0[4], d1[4], d2[4], d3[4];
-        dequant_word(w.x, zlo[r][0], zhi[r][0], d0);
-        dequant_word(w.y, zlo[r][1], zhi[r][1], d1);
-        dequant_word(w.z, zlo[r][2], zhi[r][2], d2);
-        dequant_word(w.w, zlo[r][3], zhi[r][3], d3);
-        mma_16816(accg[0], d0[0], d1[0], d0[1], d1[1], xv[q].x, xv[q].y);
-        mma_16816(accg[0], d0[2], d1[2], d0[3], d1[3], xv[q].z, xv[q].w);
-        mma_16816(accg[1], d2[0], d3[0], d2[1], d3[1], xv[q].x, xv[q].y);
-        mma_16816(accg[1], d2[2], d3[2], d2[3], d3[3], xv[q].z, xv[q].w);
-        if ((q + 1) % GP == 0) {
-#pragma unroll
-          for (int T = 0; T < 2; ++T)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              acc[T][i] = fmaf(scl[r][2 * T + (i >> 1)], accg[T][i], acc[T][i]);
-              accg[T][i] = 0.f;
-            }
-        }
-      }
+      consume_unit<GP>(L, x_base0 + st * C::kXBytes, qw_base0 + st * kQwStage,
+                       reinterpret_cast<const __half*>(s_sc + st * C::kScStride),
+                       reinterpret_cast<const uint32_t*>(s_qz + st * C::kQzStride), acc);
       fence_proxy_async_smem();  // this lane's reads of the stage precede its next TMA fill
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
@@ -1166,11 +1224,16 @@ double plan_clusters(const ClusterCaps& cc, int tiles, int upt, int want, int ma
   return best;
 }
 
+// Split-K plan of one launch: stream-K over sk.ctas CTAs (cs == 0), or nc clusters of cs CTAs.
+struct Plan {
+  StreamK sk;
+  int cs = 0, nc = 0;
+};
+
 template <int GP, bool FUSED>
-int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, const ArView* ar,
-           int max_ctas, bool early, cudaStream_t stream) {
+int make_plan(const W4Args& a, int max_ctas, Plan* out) {
+  // (every launch may take the cluster kernel: it needs no workspace partials or counters)
   using C = Cfg<GP>;
-  W4Args a = a0;
   DeviceInfo di;
   int rc = device_info(&di);
   if (rc) return rc;
@@ -1185,7 +1248,8 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
     kc.configured = true;
   }
   const int K = a.K, N = a.N;
-  StreamK sk;
+  Plan pl;
+  StreamK& sk = pl.sk;
   sk.upt = K / kUnitK;
   sk.tiles = (N + kTileN - 1) / kTileN;
   sk.total = (long long)sk.tiles * sk.upt;
@@ -1195,15 +1259,9 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
     // CTA of the same launch.
     sk.ctas = std::min(sk.ctas, di.sm_count * kc.occ);
   }
-  a.sk = sk;
 
-  CUtensorMap m_qw, m_sc, m_qz, m_x;
-  rc = encode_maps<C::RG>(a, qw, qz, sc, &m_qw, &m_sc, &m_qz, &m_x);
-  if (rc) return rc;
-  const ArView view = ar ? *ar : ArView{};
-
-  // Split-K path. The scratch-only entry point (max_ctas below the workspace bound) always takes
-  // stream-K, whose fix-up is what its scratch is for.
+  // Split-K path. Stream-K needs the partial slots and tile counters of a workspace (at most
+  // max_ctas CTAs); the cluster kernel reduces through distributed shared memory and needs none.
   // Fused launches take the cluster kernel when its exchange blocks fit the slot (N a whole
   // number of tiles) and the slot holds the 64-bit value+generation words (TP=2 down_proj shard:
   // 17.5 us, against 20.3 us for stream-K fused and 23.8 us for GEMM + NCCL). With fp32 slots
@@ -1212,7 +1270,7 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
   const bool cluster_ok = !FUSED || N % kTileN == 0;
   const bool cluster_default = !FUSED || a.ll;
   if (cluster_ok &&
-      (path == 2 || (path == 0 && cluster_default && max_ctas >= kWsMaxCtas))) {
+      (path == 2 || (path == 0 && cluster_default))) {
     const ClusterCaps* cc = nullptr;
     rc = cluster_caps<GP, FUSED>(dev, &cc);
     if (rc) return rc;
@@ -1233,15 +1291,53 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
     }
     // (the RMSNorm epilogue keeps kMaxM row sums per CTA in the workspace: kWsMaxCtas CTAs)
     if (cost > 0.0 && (path == 2 || cost <= sk_cost) && (!a.norm || nc * cs <= kWsMaxCtas)) {
-      a.cl_size = cs;
-      a.cl_count = nc;
-      return launch_kernel_clusters(w4c_kernel<GP, FUSED>, nc * cs, cs, kThreads, CfgC<GP>::kSmem,
-                                    stream, early, m_qw, m_sc, m_qz, m_x, a, view);
+      pl.cs = cs;
+      pl.nc = nc;
     }
   }
+  *out = pl;
+  return B2_OK;
+}
+
+template <int GP, bool FUSED>
+int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, const ArView* ar,
+           const Plan& pl, bool early, cudaStream_t stream) {
+  using C = Cfg<GP>;
+  W4Args a = a0;
+  a.sk = pl.sk;
+  CUtensorMap m_qw, m_sc, m_qz, m_x;
+  int rc = encode_maps<C::RG>(a, qw, qz, sc, &m_qw, &m_sc, &m_qz, &m_x);
+  if (rc) return rc;
+  const ArView view = ar ? *ar : ArView{};
+  if (pl.cs > 0) {
+    a.cl_size = pl.cs;
+    a.cl_count = pl.nc;
+    return launch_kernel_clusters(w4c_kernel<GP, FUSED>, pl.nc * pl.cs, pl.cs, kThreads,
+                                  CfgC<GP>::kSmem, stream, early, m_qw, m_sc, m_qz, m_x, a, view);
+  }
   a.cl_size = a.cl_count = 0;
-  return launch_kernel(kern, sk.ctas, kThreads, C::kSmem, stream, early, m_qw, m_sc,
-                       m_qz, m_x, a, view);
+  return launch_kernel(w4_kernel<GP, FUSED>, pl.sk.ctas, kThreads, C::kSmem, stream, early, m_qw,
+                       m_sc, m_qz, m_x, a, view);
+}
+
+// The plan of a launch for the group size in args.G.
+template <bool FUSED>
+int plan_for(const W4Args& args, int max_ctas, Plan* pl) {
+  switch (args.G) {
+    case 32: return make_plan<1, FUSED>(args, max_ctas, pl);
+    case 64: return make_plan<2, FUSED>(args, max_ctas, pl);
+    default: return make_plan<4, FUSED>(args, max_ctas, pl);
+  }
+}
+
+template <bool FUSED>
+int launch_plan(const W4Args& args, const void* qw, const void* qz, const void* sc,
+                const ArView* ar, const Plan& pl, bool early, cudaStream_t stream) {
+  switch (args.G) {
+    case 32: return launch<1, FUSED>(args, qw, qz, sc, ar, pl, early, stream);
+    case 64: return launch<2, FUSED>(args, qw, qz, sc, ar, pl, early, stream);
+    default: return launch<4, FUSED>(args, qw, qz, sc, ar, pl, early, stream);
+  }
 }
 
 int validate(const void* a, const void* qw, const void* qz, const void* sc, const void* y, int M,
@@ -1298,16 +1394,14 @@ W4Args make_args(const void* a, void* y, int M, int K, int N, int G, void* ws) {
   return r;
 }
 
-// `early`: programmatic dependent launch (the no-alloc variant, which clears its scratch with a
-// memset just before, launches normally).
+// `early`: programmatic dependent launch.
 template <bool FUSED>
 int dispatch(const W4Args& args, const void* qw, const void* qz, const void* sc, const ArView* ar,
-             cudaStream_t stream, int max_ctas = kWsMaxCtas, bool early = false) {
-  switch (args.G) {
-    case 32: return launch<1, FUSED>(args, qw, qz, sc, ar, max_ctas, early, stream);
-    case 64: return launch<2, FUSED>(args, qw, qz, sc, ar, max_ctas, early, stream);
-    default: return launch<4, FUSED>(args, qw, qz, sc, ar, max_ctas, early, stream);
-  }
+             cudaStream_t stream, bool early) {
+  Plan pl;
+  const int rc = plan_for<FUSED>(args, kWsMaxCtas, &pl);
+  if (rc) return rc;
+  return launch_plan<FUSED>(args, qw, qz, sc, ar, pl, early, stream);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -1326,30 +1420,69 @@ static_assert(kNoAllocPartialsOff % 256 == 0, "partial slots stay 256-byte align
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
-// Device address of g_noalloc_scratch, looked up once per device. In host code the name
-// g_noalloc_scratch is only a host-side stand-in for the symbol; a kernel must be given the
-// address cudaGetSymbolAddress returns for the current device.
-std::mutex g_noalloc_mu;
-unsigned char* g_noalloc_ptr[64] = {nullptr};
+// Device address of g_noalloc_scratch. In host code the name g_noalloc_scratch is only a
+// host-side stand-in for the symbol; a kernel must be given the address cudaGetSymbolAddress
+// returns in the calling thread's current context (the device's primary context for runtime-API
+// callers). The address is looked up at the first call in a context and cached per device with
+// that context's unique id, so a call from another context, or after cudaDeviceReset has replaced
+// the primary context (which reloads the module and the array), looks it up again. One lock per
+// device: threads that drive different GPUs do not wait for each other.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
 
-int noalloc_scratch(unsigned char** out) {
+template <typename Fn>
+Fn driver_fn(const char* name, int version) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion(name, &p, version, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<Fn>(p);
+}
+
+struct NoAllocEntry {
+  std::mutex mu;
+  unsigned long long ctx_id = 0;
+  unsigned char* ptr = nullptr;
+};
+NoAllocEntry g_noalloc[64];
+
+int noalloc_scratch(cudaStream_t stream, unsigned char** out) {
+  static const CtxGetCurrentFn get_ctx = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent", 12000);
+  static const CtxGetIdFn get_id = driver_fn<CtxGetIdFn>("cuCtxGetId", 12000);
   int dev = 0;
   B2_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return fail(B2_ERR_UNSUPPORTED, "w4_noalloc: device ordinal %d", dev);
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || !p)
-      return fail(B2_ERR_CUDA, "w4_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-    // The counters must start at zero; the kernel leaves them at zero after every call.
-    e = cudaMemset(p, 0, kNoAllocPartialsOff);
-    if (e == cudaSuccess) e = cudaDeviceSynchronize();
-    if (e != cudaSuccess)
-      return fail(B2_ERR_CUDA, "w4_noalloc: clearing the scratch failed: %s", cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_ctx || !get_id || get_ctx(&ctx) != CUDA_SUCCESS)
+    return fail(B2_ERR_CUDA, "w4_noalloc: cannot query the current CUDA context");
+  if (!ctx) {  // no context current on this thread yet: make the device's primary context current
+    B2_CUDA_TRY(cudaSetDevice(dev));
+    if (get_ctx(&ctx) != CUDA_SUCCESS || !ctx)
+      return fail(B2_ERR_CUDA, "w4_noalloc: no CUDA context on device %d", dev);
   }
-  *out = g_noalloc_ptr[dev];
+  if (get_id(ctx, &id) != CUDA_SUCCESS)
+    return fail(B2_ERR_CUDA, "w4_noalloc: cannot identify the current CUDA context");
+  NoAllocEntry& e = g_noalloc[dev];
+  std::lock_guard<std::mutex> lk(e.mu);
+  if (!e.ptr || e.ctx_id != id) {
+    // The set-up: not inside a stream capture, where looking up a symbol may load the module.
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    B2_CUDA_TRY(cudaStreamIsCapturing(stream, &cs));
+    if (cs != cudaStreamCaptureStatusNone)
+      return fail(B2_ERR_STATE,
+                  "w4_noalloc: the first call in a CUDA context looks up the scratch array and "
+                  "must come before any stream capture (make one eager call first)");
+    void* p = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (err != cudaSuccess || !p)
+      return fail(B2_ERR_CUDA, "w4_noalloc: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(err));
+    e.ptr = static_cast<unsigned char*>(p);
+    e.ctx_id = id;
+  }
+  *out = e.ptr;
   return B2_OK;
 }
 
@@ -1360,7 +1493,7 @@ int launch_w4(const void* a, const void* qw, const void* qz, const void* sc, voi
   int rc = validate(a, qw, qz, sc, y, M, K, N, G, ws, ws_bytes);
   if (rc) return rc;
   return dispatch<false>(make_args(a, y, M, K, N, G, ws), qw, qz, sc, nullptr, stream,
-                         kWsMaxCtas, /*early=*/true);
+                         /*early=*/true);
 }
 
 int launch_w4_noalloc(const void* a, const void* qw, const void* qz, const void* sc, void* y, int M,
@@ -1373,16 +1506,30 @@ int launch_w4_noalloc(const void* a, const void* qw, const void* qz, const void*
   unsigned char* scratch = nullptr;
   int rc = validate(a, qw, qz, sc, y, M, K, N, G);
   if (rc) return rc;
-  rc = noalloc_scratch(&scratch);
+  rc = noalloc_scratch(stream, &scratch);
   if (rc) return rc;
   W4Args args = make_args(a, y, M, K, N, G, scratch);
   args.status = reinterpret_cast<int*>(scratch);
   args.counters = reinterpret_cast<int*>(scratch + kNoAllocCountersOff);
   args.partials = reinterpret_cast<float*>(scratch + kNoAllocPartialsOff);
-  // Clear the status word and the counters this call uses: the array keeps whatever the last
-  // call left, and a call that gave up on a wait may have left counters behind.
+  Plan pl;
+  rc = plan_for<false>(args, kNoAllocMaxCtas, &pl);
+  if (rc) return rc;
+  if (pl.cs > 0)  // the cluster kernel uses none of the scratch: launched as b2_w4_gemm launches it
+    return launch_plan<false>(args, qw, qz, sc, nullptr, pl, /*early=*/true, stream);
+  // Stream-K: clear the status word and the counters this call uses first. The array keeps
+  // whatever the last call left, and a call that gave up on a wait may have left counters behind.
   B2_CUDA_TRY(cudaMemsetAsync(scratch, 0, kNoAllocCountersOff + (size_t)tiles * 4, stream));
-  return dispatch<false>(args, qw, qz, sc, nullptr, stream, kNoAllocMaxCtas);
+  return launch_plan<false>(args, qw, qz, sc, nullptr, pl, /*early=*/false, stream);
+}
+
+int noalloc_scratch_info(void** ptr, size_t* bytes) {
+  unsigned char* p = nullptr;
+  const int rc = noalloc_scratch(nullptr, &p);
+  if (rc) return rc;
+  *ptr = p;
+  *bytes = kNoAllocBytes;
+  return B2_OK;
 }
 
 // `residual` and `nw` non-null: the residual add + RMSNorm epilogue (see norm_rstd).
@@ -1434,7 +1581,7 @@ int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* q
   // CTAs (42 fit an idle GPU), fewer than 40 could then be resident together and back-to-back
   // launches ran their barrier into the timeout. A kernel after this one may still start early:
   // by then every CTA of this grid is resident.
-  return dispatch<true>(args, qw, qz, sc, &v, stream, kWsMaxCtas, /*early=*/!norm);
+  return dispatch<true>(args, qw, qz, sc, &v, stream, /*early=*/!norm);
 }
 
 }  // namespace b2
@@ -1471,4 +1618,30 @@ extern "C" int b2_w4_gemm_noalloc(const void* a, const void* qw, const void* qz,
                                   void* y, int M, int K, int N, int group_size, void* stream) {
   return b2::launch_w4_noalloc(a, qw, qz, sc, y, M, K, N, group_size,
                                static_cast<cudaStream_t>(stream));
+}
+
+// Address and size of the no-alloc scratch array on the current device; see include/b2_skinny.h.
+extern "C" int b2_w4_noalloc_scratch(void** device_ptr, size_t* bytes) {
+  if (!device_ptr || !bytes) return b2::fail(B2_ERR_INVALID_ARG, "w4_noalloc_scratch: null output");
+  return b2::noalloc_scratch_info(device_ptr, bytes);
+}
+
+// The split-K plan of a W4 launch; see include/b2_skinny.h.
+extern "C" int b2_w4_plan(int M, int K, int N, int group_size, int fused, int* path, int* cluster,
+                          int* ctas) {
+  if (!path || !cluster || !ctas) return b2::fail(B2_ERR_INVALID_ARG, "w4_plan: null output");
+  const int fake = 256;  // validation needs aligned non-null pointers; nothing is dereferenced
+  const void* p = reinterpret_cast<const void*>((uintptr_t)fake);
+  int rc = b2::validate(p, p, p, p, p, M, K, N, group_size);
+  if (rc) return rc;
+  b2::W4Args a = b2::make_args(p, const_cast<void*>(p), M, K, N, group_size, nullptr);
+  a.ll = fused ? 1 : 0;
+  b2::Plan pl;
+  rc = fused ? b2::plan_for<true>(a, b2::kWsMaxCtas, &pl)
+             : b2::plan_for<false>(a, b2::kWsMaxCtas, &pl);
+  if (rc) return rc;
+  *path = pl.cs > 0 ? 2 : 1;
+  *cluster = pl.cs;
+  *ctas = pl.cs > 0 ? pl.cs * pl.nc : pl.sk.ctas;
+  return B2_OK;
 }
