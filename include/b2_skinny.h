@@ -231,6 +231,34 @@ int b2_nvar_world(const b2_nvar* ar);
 int b2_nvar_destroy(b2_nvar* ar);
 
 /* ------------------------------------------------------------------------------------------
+ * Several ranks of one tensor-parallel group emulated on one GPU (testing support; no counterpart
+ * in the reference)
+ *
+ * The multi-rank exchange of the all-reduce and of the fused GEMM epilogues can be exercised on a
+ * machine with one GPU: `ranks` handles created in one process on one device (b2_nvar_create with
+ * rank r of world `ranks`, r = 0..ranks-1) are connected to one another's buffers directly, and
+ * one launch runs every rank's CTAs (grid.y = rank), each rank with its own operands, workspace
+ * and handle. The ranks' CTAs wait for one another, so the launch is cooperative: either all of
+ * them are resident at once or the launch fails (B2_ERR_CUDA); each rank's grid is planned on
+ * 1/ranks of the GPU. Results are those of `ranks` GPUs running the ordinary entry points, except
+ * that the split-K plan (and so the fp32 rounding of the partial sums) is that of a GPU with
+ * 1/ranks of the SMs. 1 <= ranks <= 4.
+ * ---------------------------------------------------------------------------------------- */
+/* Connect handles[0..ranks-1] (rank r = handles[r], all on one device) to one another. */
+int b2_nvar_connect_local(b2_nvar* const* handles, int ranks);
+/* b2_nvar_allreduce of every rank in one launch: out[r] = sum over ranks of in[q] (rank order). */
+int b2_nvar_allreduce_emulated(b2_nvar* const* handles, int ranks, const void* const* in,
+                               void* const* out, size_t count, int dtype, void* stream);
+/* b2_w4_gemm_allreduce (residual == norm_weight == NULL) or b2_w4_gemm_allreduce_rmsnorm of every
+ * rank in one launch; every array holds one pointer per rank. */
+int b2_w4_gemm_allreduce_emulated(b2_nvar* const* handles, int ranks, const void* const* a,
+                                  const void* const* qw, const void* const* qz,
+                                  const void* const* sc, void* const* residual,
+                                  const void* const* norm_weight, float eps, void* const* y, int M,
+                                  int K, int N, int group_size, void* const* ws, size_t ws_bytes,
+                                  void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * Tuning (process-wide; for measurement sweeps). B2_TUNE="key=value,..." in the environment
  * presets keys before first use; b2_set_tuning overrides them.
  * ---------------------------------------------------------------------------------------- */
@@ -242,6 +270,11 @@ int b2_nvar_destroy(b2_nvar* ar);
                                      fix-up, 2 = thread-block clusters reducing through
                                      distributed shared memory                                   */
 #define B2_TUNE_W4_CLUSTER 5      /* cluster path: CTAs per cluster (0 = chosen per shape)      */
+#define B2_TUNE_AR_FLAGS 6        /* fused all-reduce: nonzero sends fp32 values published by
+                                     per-tile flags instead of 64-bit (generation, value) words  */
+#define B2_TUNE_AR_TWO_SHOT 7     /* fused all-reduce in the cluster kernel: 0 = two-shot from 4
+                                     ranks up (each tile reduced at one owner rank, the result
+                                     sent back), 1 = always two-shot, 2 = always one-shot        */
 int b2_set_tuning(int key, int value);
 int b2_get_tuning(int key);
 

@@ -28,6 +28,11 @@ B2_DTYPE_F32 = 1
 B2_BLOB_BYTES = 64
 B2_TUNE_CTAS_PER_SM = 1
 B2_TUNE_MIN_UNITS = 2
+B2_TUNE_NO_PDL = 3
+B2_TUNE_W4_PATH = 4
+B2_TUNE_W4_CLUSTER = 5
+B2_TUNE_AR_FLAGS = 6
+B2_TUNE_AR_TWO_SHOT = 7
 
 _vp, _i, _sz, _u64 = C.c_void_p, C.c_int, C.c_size_t, C.c_uint64
 _SIGS = {
@@ -60,6 +65,13 @@ _SIGS = {
     "b2_nvar_rank": (_i, [_vp]),
     "b2_nvar_world": (_i, [_vp]),
     "b2_nvar_destroy": (_i, [_vp]),
+    "b2_nvar_connect_local": (_i, [C.POINTER(_vp), _i]),
+    "b2_nvar_allreduce_emulated": (_i, [C.POINTER(_vp), _i, C.POINTER(_vp), C.POINTER(_vp), _sz,
+                                        _i, _vp]),
+    "b2_w4_gemm_allreduce_emulated": (_i, [C.POINTER(_vp), _i, C.POINTER(_vp), C.POINTER(_vp),
+                                           C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_vp),
+                                           C.POINTER(_vp), C.c_float, C.POINTER(_vp), _i, _i, _i,
+                                           _i, C.POINTER(_vp), _sz, _vp]),
     "b2_set_tuning": (_i, [_i, _i]),
     "b2_get_tuning": (_i, [_i]),
     "b2_w4_plan": (_i, [_i, _i, _i, _i, _i, C.POINTER(_i), C.POINTER(_i), C.POINTER(_i)]),
@@ -112,3 +124,8 @@ def w4_plan(M: int, K: int, N: int, G: int, fused: bool = False) -> dict:
                            C.byref(ctas)), "b2_w4_plan")
     kernel = "w4c_kernel" if path.value == 2 else "w4_kernel"
     return {"kernel": kernel, "path": path.value, "cluster": cs.value, "ctas": ctas.value}
+
+
+def ptr_array(ptrs) -> "C.Array":
+    """A C array of void* (for the entry points that take one pointer per rank); None -> NULL."""
+    return (_vp * len(ptrs))(*[p if p is None else int(p) for p in ptrs])

@@ -71,9 +71,8 @@ __device__ __forceinline__ uint4 pack_vec(const float (&acc)[8], bool is_half) {
 // CTA c owns bytes [c*chunk, (c+1)*chunk) of the payload and flag index c. (The 64-bit word
 // exchange of the fused GEMM epilogue measured slower here, 13.8 against ~10 us at 80 KB and
 // P = 2: with one vector per thread the fence is cheaper than four times the bytes.)
-__global__ void __launch_bounds__(kThreads) nvar_kernel(const uint4* in, uint4* out, size_t nvec,
-                                                        size_t chunk_vec, int is_half,
-                                                        const ArView v) {
+__device__ __forceinline__ void nvar_body(const uint4* in, uint4* out, size_t nvec,
+                                          size_t chunk_vec, int is_half, const ArView& v) {
   __shared__ uint32_t s_gen;
   if (threadIdx.x == 0) s_gen = ar_begin(v);
   __syncthreads();
@@ -106,6 +105,26 @@ __global__ void __launch_bounds__(kThreads) nvar_kernel(const uint4* in, uint4* 
   }
   __syncthreads();
   if (threadIdx.x == 0) ar_finish(v, e);
+}
+
+__global__ void __launch_bounds__(kThreads) nvar_kernel(const uint4* in, uint4* out, size_t nvec,
+                                                        size_t chunk_vec, int is_half,
+                                                        const __grid_constant__ ArView v) {
+  nvar_body(in, out, nvec, chunk_vec, is_half, v);
+}
+
+// Several ranks of one group on this GPU in one cooperative launch (grid.y = rank), for tests.
+constexpr int kEmuMaxRanks = 4;
+struct NvarEmu {
+  const uint4* in[kEmuMaxRanks];
+  uint4* out[kEmuMaxRanks];
+  ArView ar[kEmuMaxRanks];
+  size_t nvec, chunk_vec;
+  int is_half;
+};
+__global__ void __launch_bounds__(kThreads) nvar_kernel_emu(const __grid_constant__ NvarEmu E) {
+  const int r = blockIdx.y;
+  nvar_body(E.in[r], E.out[r], E.nvec, E.chunk_vec, E.is_half, E.ar[r]);
 }
 
 unsigned long long default_timeout_ns() {
@@ -151,6 +170,30 @@ int nvar_view(b2_nvar* h, ArView* out, size_t need_slot_bytes, int* tiles_cap) {
   v.timeout_ns = h->timeout_ns;
   *out = v;
   if (tiles_cap) *tiles_cap = kArMaxFlags;
+  return B2_OK;
+}
+
+// Checks of one all-reduce call and its grid: one CTA per chunk of at least 8 KB.
+int nvar_prepare(b2_nvar* h, const void* in, const void* out, size_t count, int dtype, ArView* v,
+                 size_t* nvec, size_t* chunk_vec, size_t* grid) {
+  if (!in || !out) return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: null pointer");
+  if (dtype != B2_DTYPE_F16 && dtype != B2_DTYPE_F32)
+    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: dtype %d (0 = f16, 1 = f32)", dtype);
+  const size_t bytes = count * (dtype == B2_DTYPE_F16 ? 2 : 4);
+  if (bytes == 0 || bytes % 16 != 0)
+    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: %zu bytes (must be a positive multiple of 16)",
+                bytes);
+  if (!aligned16(in) || !aligned16(out))
+    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: buffers must be 16-byte aligned");
+  int rc = nvar_view(h, v, bytes, nullptr);
+  if (rc) return rc;
+  *nvec = bytes / 16;
+  size_t chunk = std::max(kMinChunk, (bytes + 147) / 148);
+  chunk = (chunk + 15) & ~(size_t)15;
+  *chunk_vec = chunk / 16;
+  *grid = (*nvec + *chunk_vec - 1) / *chunk_vec;
+  if (*grid > (size_t)kArMaxFlags)
+    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: too many chunks");
   return B2_OK;
 }
 
@@ -234,27 +277,65 @@ int b2_nvar_set_timeout_ns(b2_nvar* h, uint64_t ns) {
 
 int b2_nvar_allreduce(b2_nvar* h, const void* in, void* out, size_t count, int dtype,
                       void* stream) {
-  if (!in || !out) return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: null pointer");
-  if (dtype != B2_DTYPE_F16 && dtype != B2_DTYPE_F32)
-    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: dtype %d (0 = f16, 1 = f32)", dtype);
-  const size_t bytes = count * (dtype == B2_DTYPE_F16 ? 2 : 4);
-  if (bytes == 0 || bytes % 16 != 0)
-    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: %zu bytes (must be a positive multiple of 16)",
-                bytes);
-  if (!aligned16(in) || !aligned16(out))
-    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: buffers must be 16-byte aligned");
   ArView v;
-  int rc = nvar_view(h, &v, bytes, nullptr);
+  size_t nvec = 0, chunk_vec = 0, grid = 0;
+  int rc = nvar_prepare(h, in, out, count, dtype, &v, &nvec, &chunk_vec, &grid);
   if (rc) return rc;
-  const size_t nvec = bytes / 16;
-  size_t chunk = std::max(kMinChunk, (bytes + 147) / 148);
-  chunk = (chunk + 15) & ~(size_t)15;
-  const size_t chunk_vec = chunk / 16;
-  const size_t grid = (nvec + chunk_vec - 1) / chunk_vec;
-  if (grid > (size_t)kArMaxFlags) return fail(B2_ERR_INVALID_ARG, "nvar_allreduce: too many chunks");
   nvar_kernel<<<(unsigned)grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(in), static_cast<uint4*>(out), nvec, chunk_vec,
       dtype == B2_DTYPE_F16 ? 1 : 0, v);
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+
+int b2_nvar_connect_local(b2_nvar* const* handles, int ranks) {
+  if (!handles || ranks < 1 || ranks > kEmuMaxRanks)
+    return fail(B2_ERR_INVALID_ARG, "nvar_connect_local: %d ranks (1..%d)", ranks, kEmuMaxRanks);
+  for (int r = 0; r < ranks; ++r) {
+    const b2_nvar* h = handles[r];
+    if (!h || h->rank != r || h->world != ranks || h->device != handles[0]->device)
+      return fail(B2_ERR_INVALID_ARG,
+                  "nvar_connect_local: handle %d must be rank %d of %d on device %d", r, r, ranks,
+                  handles[0] ? handles[0]->device : -1);
+    if (h->slot_cap != handles[0]->slot_cap)
+      return fail(B2_ERR_INVALID_ARG, "nvar_connect_local: the handles' slots differ in size");
+  }
+  for (int r = 0; r < ranks; ++r) {
+    for (int q = 0; q < ranks; ++q) handles[r]->peers[q] = handles[q]->local;
+    handles[r]->connected = true;
+  }
+  return B2_OK;
+}
+
+int b2_nvar_allreduce_emulated(b2_nvar* const* handles, int ranks, const void* const* in,
+                               void* const* out, size_t count, int dtype, void* stream) {
+  if (!handles || !in || !out || ranks < 1 || ranks > kEmuMaxRanks)
+    return fail(B2_ERR_INVALID_ARG, "nvar_allreduce_emulated: %d ranks (1..%d)", ranks,
+                kEmuMaxRanks);
+  NvarEmu E;
+  memset(&E, 0, sizeof(E));
+  size_t grid = 0;
+  for (int r = 0; r < ranks; ++r) {
+    int rc = nvar_prepare(handles[r], in[r], out[r], count, dtype, &E.ar[r], &E.nvec,
+                          &E.chunk_vec, &grid);
+    if (rc) return rc;
+    if (E.ar[r].rank != r || E.ar[r].world != ranks)
+      return fail(B2_ERR_STATE, "nvar_allreduce_emulated: handle %d is rank %d of %d", r,
+                  E.ar[r].rank, E.ar[r].world);
+    E.in[r] = static_cast<const uint4*>(in[r]);
+    E.out[r] = static_cast<uint4*>(out[r]);
+  }
+  E.is_half = dtype == B2_DTYPE_F16 ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, (unsigned)ranks);
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, nvar_kernel_emu, E));
   B2_CUDA_TRY(cudaGetLastError());
   return B2_OK;
 }

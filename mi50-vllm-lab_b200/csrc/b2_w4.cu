@@ -30,6 +30,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "b2_device.cuh"
@@ -90,7 +91,9 @@ struct W4Args {
   int* counters;
   int* status;
   int cl_size, cl_count;  // cluster kernel: CTAs per cluster, clusters
-  int ll;                 // fused stream-K: exchange as 64-bit value+generation words
+  int ll;                 // fused: exchange as 64-bit value+generation words
+  int two_shot;           // fused cluster kernel with ll: reduce at the tile's owner rank, then
+                          // send the result back (instead of every rank reducing every tile)
   // fused launches only: residual add + RMSNorm of the all-reduced rows (norm != 0)
   int norm;
   float eps;
@@ -483,10 +486,9 @@ __device__ __forceinline__ bool norm_rstd(const W4Args& p, const ArView& ar, uin
 // group is scaled once: acc += s * sum. Every weight is dequantized once per CTA and used for all
 // M rows.
 template <int GP, bool FUSED>
-__global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
-    w4_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_sc,
-              const __grid_constant__ CUtensorMap tm_qz, const __grid_constant__ CUtensorMap tm_x,
-              const W4Args p, const ArView ar) {
+__device__ __forceinline__ void w4_body(const CUtensorMap& tm_qw, const CUtensorMap& tm_sc,
+                                        const CUtensorMap& tm_qz, const CUtensorMap& tm_x,
+                                        const W4Args& p, const ArView& ar) {
   using C = Cfg<GP>;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -793,6 +795,14 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
   }
 }
 
+template <int GP, bool FUSED>
+__global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
+    w4_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_sc,
+              const __grid_constant__ CUtensorMap tm_qz, const __grid_constant__ CUtensorMap tm_x,
+              const __grid_constant__ W4Args p, const __grid_constant__ ArView ar) {
+  w4_body<GP, FUSED>(tm_qw, tm_sc, tm_qz, tm_x, p, ar);
+}
+
 // =================================================================================================
 // Cluster split-K variant. The CTAs of one thread-block cluster share output tiles: cluster c
 // owns tiles c, c + NC, ... and CTA rank r of the cluster computes k-units
@@ -823,10 +833,9 @@ struct CfgC {
 };
 
 template <int GP, bool FUSED>
-__global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
-    w4c_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_sc,
-               const __grid_constant__ CUtensorMap tm_qz, const __grid_constant__ CUtensorMap tm_x,
-               const W4Args p, const ArView ar) {
+__device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtensorMap& tm_sc,
+                                        const CUtensorMap& tm_qz, const CUtensorMap& tm_x,
+                                        const W4Args& p, const ArView& ar) {
   using C = CfgC<GP>;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
@@ -1018,7 +1027,10 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
           // (tile * 128 + c0) * M, element idx in the order the threads produce them, so a
           // warp's pushes over NVLink are coalesced (needs N % 128 == 0, checked on the host)
           const size_t at = ((size_t)tile * kTileN + c0) * p.M + idx;
-          if (p.ll) {
+          if (p.ll && p.two_shot) {  // to the tile's owner only (possibly this rank)
+            ll_store(reinterpret_cast<uint64_t*>(ar_slot(ar, tile % ar.world, e & 1u, ar.rank)) + at,
+                     s, e);
+          } else if (p.ll) {
             for (int r = 0; r < ar.world; ++r)
               ll_store(reinterpret_cast<uint64_t*>(ar_slot(ar, r, e & 1u, ar.rank)) + at, s, e);
           } else {
@@ -1048,22 +1060,44 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
       const size_t blk = ((size_t)tile * kTileN + c0) * p.M;
       if (p.ll) {
         bool got = true;
+        // Two-shot: the owner of the tile has every rank's partial of it in its slots; it adds
+        // them and sends the fp16 result (as an exactly representable fp32 word) to the other
+        // ranks' slot of the owner, at the same offsets: no rank sends partials of a tile it
+        // owns, so those words are free. One-shot: every rank has every rank's partials.
+        const int owner = tile % ar.world;
+        const bool wait_result = p.two_shot && owner != ar.rank;
         for (int idx = tid; idx < p.M * W; idx += kWarps * 32) {
           const int m = idx / W, col = c0 + (idx - m * W);
           const int n = tile * kTileN + col;
           if (n >= p.N) continue;
-          const uint64_t* ptr[kArMaxWorld];
+          __half yh;
+          if (wait_result) {
+            const uint64_t* ptr[1] = {
+                reinterpret_cast<const uint64_t*>(ar_slot(ar, ar.rank, e & 1u, owner)) + blk + idx};
+            float a[1];
+            got &= ll_gather<1>(ptr, 1, e, deadline, a);
+            yh = __float2half_rn(a[0]);
+          } else {
+            const uint64_t* ptr[kArMaxWorld];
 #pragma unroll
-          for (int src = 0; src < kArMaxWorld; ++src)
-            ptr[src] = reinterpret_cast<const uint64_t*>(
-                           ar_slot(ar, ar.rank, e & 1u, src < ar.world ? src : 0)) + blk + idx;
-          float a[kArMaxWorld];
-          got &= ll_gather<kArMaxWorld>(ptr, ar.world, e, deadline, a);
-          float s = 0.f;
+            for (int src = 0; src < kArMaxWorld; ++src)
+              ptr[src] = reinterpret_cast<const uint64_t*>(
+                             ar_slot(ar, ar.rank, e & 1u, src < ar.world ? src : 0)) + blk + idx;
+            float a[kArMaxWorld];
+            got &= ll_gather<kArMaxWorld>(ptr, ar.world, e, deadline, a);
+            float s = 0.f;
 #pragma unroll
-          for (int src = 0; src < kArMaxWorld; ++src)
-            if (src < ar.world) s += a[src];
-          const __half yh = __float2half_rn(s);
+            for (int src = 0; src < kArMaxWorld; ++src)
+              if (src < ar.world) s += a[src];
+            yh = __float2half_rn(s);
+            if (p.two_shot) {
+              const float v = __half2float(yh);
+              for (int r = 0; r < ar.world; ++r)
+                if (r != ar.rank)
+                  ll_store(reinterpret_cast<uint64_t*>(ar_slot(ar, r, e & 1u, ar.rank)) + blk + idx,
+                           v, e);
+            }
+          }
           p.y[(size_t)m * p.N + n] = yh;
           if (p.norm) {
             const float x = norm_x(yh, p.res[(size_t)m * p.N + n]);
@@ -1122,6 +1156,39 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
     ok = ok && *s_flag;
   }
   if (!ok && lane == 0) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
+}
+
+template <int GP, bool FUSED>
+__global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
+    w4c_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_sc,
+               const __grid_constant__ CUtensorMap tm_qz, const __grid_constant__ CUtensorMap tm_x,
+               const __grid_constant__ W4Args p, const __grid_constant__ ArView ar) {
+  w4c_body<GP, FUSED>(tm_qw, tm_sc, tm_qz, tm_x, p, ar);
+}
+
+// =================================================================================================
+// Several ranks of a tensor-parallel group emulated on one GPU, in one launch: grid.y = rank, and
+// every rank's operands, tensor maps and all-reduce view are kernel arguments indexed by it. The
+// ranks' CTAs wait for one another, so the launch is cooperative: either all of them are resident
+// at once or the launch fails. For testing the multi-rank exchange without several GPUs.
+// =================================================================================================
+constexpr int kEmuMaxRanks = 4;
+struct W4Emu {
+  CUtensorMap qw[kEmuMaxRanks], sc[kEmuMaxRanks], qz[kEmuMaxRanks], x[kEmuMaxRanks];
+  W4Args p[kEmuMaxRanks];
+  ArView ar[kEmuMaxRanks];
+};
+
+template <int GP>
+__global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3) w4_kernel_emu(const __grid_constant__ W4Emu E) {
+  const int r = blockIdx.y;
+  w4_body<GP, true>(E.qw[r], E.sc[r], E.qz[r], E.x[r], E.p[r], E.ar[r]);
+}
+
+template <int GP>
+__global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3) w4c_kernel_emu(const __grid_constant__ W4Emu E) {
+  const int r = blockIdx.y;
+  w4c_body<GP, true>(E.qw[r], E.sc[r], E.qz[r], E.x[r], E.p[r], E.ar[r]);
 }
 
 struct KernelCache {
@@ -1205,11 +1272,11 @@ int cluster_caps(int dev, const ClusterCaps** out) {
 // reduction when the tile is split). Returns the cost in unit-times, or a negative value when no
 // cluster size fits.
 double plan_clusters(const ClusterCaps& cc, int tiles, int upt, int want, int max_cs, int* cs_out,
-                     int* nc_out) {
+                     int* nc_out, int share = 1) {
   double best = -1.0;
   for (int cs = 1; cs <= 16 && cs <= upt && cs <= max_cs; ++cs) {
     if (want > 0 && cs != want) continue;
-    const int ncmax = cc.max_clusters[cs];
+    const int ncmax = cc.max_clusters[cs] / share;
     if (ncmax < 1) continue;
     const int nc = std::min(tiles, ncmax);
     const int per_cluster = (tiles + nc - 1) / nc;
@@ -1230,8 +1297,9 @@ struct Plan {
   int cs = 0, nc = 0;
 };
 
+// `share`: the launch gets 1/share of the GPU (several emulated ranks in one launch).
 template <int GP, bool FUSED>
-int make_plan(const W4Args& a, int max_ctas, Plan* out) {
+int make_plan(const W4Args& a, int max_ctas, Plan* out, int share = 1) {
   // (every launch may take the cluster kernel: it needs no workspace partials or counters)
   using C = Cfg<GP>;
   DeviceInfo di;
@@ -1257,7 +1325,7 @@ int make_plan(const W4Args& a, int max_ctas, Plan* out) {
   if (FUSED) {
     // Every CTA must be resident at once: a CTA waiting for peers must not hold back another
     // CTA of the same launch.
-    sk.ctas = std::min(sk.ctas, di.sm_count * kc.occ);
+    sk.ctas = std::min(sk.ctas, std::max(1, di.sm_count * kc.occ / share));
   }
 
   // Split-K path. Stream-K needs the partial slots and tile counters of a workspace (at most
@@ -1276,8 +1344,11 @@ int make_plan(const W4Args& a, int max_ctas, Plan* out) {
     if (rc) return rc;
     int cs = 0, nc = 0;
     const int max_cs = 16;
-    const double cost =
-        plan_clusters(*cc, sk.tiles, sk.upt, tuning(B2_TUNE_W4_CLUSTER), max_cs, &cs, &nc);
+    // B2_TUNE_CTAS_PER_SM below the kernel's occupancy caps the resident clusters likewise
+    const int cps = tuning(B2_TUNE_CTAS_PER_SM);
+    const int occ_share = (cps > 0 && cps < kc.occ) ? share * kc.occ / cps : share;
+    const double cost = plan_clusters(*cc, sk.tiles, sk.upt, tuning(B2_TUNE_W4_CLUSTER), max_cs,
+                                      &cs, &nc, occ_share);
     // stream-K: even units per CTA, plus the tail of the CTAs that finish a shared tile
     const long long per_cta = (sk.total + sk.ctas - 1) / sk.ctas;
     const double sk_cost = (double)per_cta + ((sk.total % sk.upt == 0 && sk.ctas <= sk.tiles &&
@@ -1322,11 +1393,11 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
 
 // The plan of a launch for the group size in args.G.
 template <bool FUSED>
-int plan_for(const W4Args& args, int max_ctas, Plan* pl) {
+int plan_for(const W4Args& args, int max_ctas, Plan* pl, int share = 1) {
   switch (args.G) {
-    case 32: return make_plan<1, FUSED>(args, max_ctas, pl);
-    case 64: return make_plan<2, FUSED>(args, max_ctas, pl);
-    default: return make_plan<4, FUSED>(args, max_ctas, pl);
+    case 32: return make_plan<1, FUSED>(args, max_ctas, pl, share);
+    case 64: return make_plan<2, FUSED>(args, max_ctas, pl, share);
+    default: return make_plan<4, FUSED>(args, max_ctas, pl, share);
   }
 }
 
@@ -1386,6 +1457,7 @@ W4Args make_args(const void* a, void* y, int M, int K, int N, int G, void* ws) {
   r.partials = reinterpret_cast<float*>(wsb + ws_partials_offset());
   r.cl_size = r.cl_count = 0;
   r.ll = 0;
+  r.two_shot = 0;
   r.norm = 0;
   r.eps = 0.f;
   r.nw = nullptr;
@@ -1532,11 +1604,11 @@ int noalloc_scratch_info(void** ptr, size_t* bytes) {
   return B2_OK;
 }
 
-// `residual` and `nw` non-null: the residual add + RMSNorm epilogue (see norm_rstd).
-int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* qz, const void* sc,
-                        void* y, int M, int K, int N, int G, void* ws, size_t ws_bytes,
-                        cudaStream_t stream, void* residual = nullptr, const void* nw = nullptr,
-                        float eps = 0.f) {
+// Checks and kernel arguments of one rank's fused launch. `residual` and `nw` non-null: the
+// residual add + RMSNorm epilogue (see norm_rstd).
+int fused_args(b2_nvar* h, const void* a, const void* qw, const void* qz, const void* sc, void* y,
+               int M, int K, int N, int G, void* ws, size_t ws_bytes, void* residual,
+               const void* nw, float eps, W4Args* out, ArView* view) {
   int rc = validate(a, qw, qz, sc, y, M, K, N, G, ws, ws_bytes);
   if (rc) return rc;
   const bool norm = residual || nw;
@@ -1556,18 +1628,21 @@ int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* q
     if (!(eps >= 0.f) || eps > 1.f)
       return fail(B2_ERR_INVALID_ARG, "w4_allreduce_rmsnorm: eps %g outside [0, 1]", (double)eps);
   }
-  ArView v;
   int tiles_cap = 0;
-  rc = nvar_view(h, &v, (size_t)M * N * sizeof(float), &tiles_cap);
+  rc = nvar_view(h, view, (size_t)M * N * sizeof(float), &tiles_cap);
   if (rc) return rc;
   if ((N + kTileN - 1) / kTileN > tiles_cap)
     return fail(B2_ERR_INVALID_ARG, "w4_allreduce: N=%d has more tiles than flags", N);
-  // Early launch is safe here too: the generation is read after griddepcontrol.wait, and a
-  // dependent grid starts only once every CTA of this one is resident, so none of the CTAs that
-  // wait for peers in the second phase can be held back.
   W4Args args = make_args(a, y, M, K, N, G, ws);
-  // the low-latency exchange needs 8 bytes per output element in each slot
-  args.ll = v.slot_bytes >= (unsigned long long)M * N * 8 ? 1 : 0;
+  // the low-latency exchange needs 8 bytes per output element in each slot (the handle allocates
+  // 4x the payload it was created for, so it always has them); B2_TUNE_AR_FLAGS selects the fp32
+  // values + per-tile flags form instead
+  args.ll = (view->slot_bytes >= (unsigned long long)M * N * 8 && tuning(B2_TUNE_AR_FLAGS) == 0)
+                ? 1 : 0;
+  // Two-shot moves 2 (P-1)/P of the payload per rank over NVLink instead of P-1 times it, for one
+  // more hop of latency: the choice from 4 ranks up (B2_TUNE_AR_TWO_SHOT: 1 on, 2 off).
+  const int ts = tuning(B2_TUNE_AR_TWO_SHOT);
+  args.two_shot = args.ll && (ts == 1 || (ts == 0 && view->world >= 4)) ? 1 : 0;
   if (norm) {
     args.norm = 1;
     args.eps = eps;
@@ -1575,13 +1650,107 @@ int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* q
     args.nw = static_cast<const __half*>(nw);
     args.npart = reinterpret_cast<float*>(static_cast<char*>(ws) + ws_norm_offset());
   }
+  *out = args;
+  return B2_OK;
+}
+
+int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* qz, const void* sc,
+                        void* y, int M, int K, int N, int G, void* ws, size_t ws_bytes,
+                        cudaStream_t stream, void* residual = nullptr, const void* nw = nullptr,
+                        float eps = 0.f) {
+  W4Args args;
+  ArView v;
+  const int rc = fused_args(h, a, qw, qz, sc, y, M, K, N, G, ws, ws_bytes, residual, nw, eps,
+                            &args, &v);
+  if (rc) return rc;
+  // Early launch is safe here too: the generation is read after griddepcontrol.wait, and a
+  // dependent grid starts only once every CTA of this one is resident, so none of the CTAs that
+  // wait for peers in the second phase can be held back.
   // The RMSNorm epilogue's grid-wide barrier needs every CTA resident at once, so that launch
   // starts only after the previous kernel has finished. Launched early, a grid's first clusters
   // take whatever slots the previous grid leaves free; measured on B200 with 40 clusters of 12
   // CTAs (42 fit an idle GPU), fewer than 40 could then be resident together and back-to-back
   // launches ran their barrier into the timeout. A kernel after this one may still start early:
   // by then every CTA of this grid is resident.
-  return dispatch<true>(args, qw, qz, sc, &v, stream, /*early=*/!norm);
+  return dispatch<true>(args, qw, qz, sc, &v, stream, /*early=*/!args.norm);
+}
+
+// `R` ranks of one group in one cooperative launch on this GPU (grid.y = rank). Every rank gets
+// 1/R of the GPU in the plan, and the cooperative attribute makes the launch fail rather than
+// start with CTAs that cannot all be resident.
+template <int GP>
+int launch_emu(const W4Args* args, const ArView* views, const void* const* qw,
+               const void* const* qz, const void* const* sc, int R, cudaStream_t stream) {
+  using C = Cfg<GP>;
+  Plan pl;
+  int rc = make_plan<GP, true>(args[0], kWsMaxCtas, &pl, R);
+  if (rc) return rc;
+  W4Emu E;
+  memset(&E, 0, sizeof(E));
+  for (int r = 0; r < R; ++r) {
+    W4Args a = args[r];
+    a.sk = pl.sk;
+    a.cl_size = pl.cs;
+    a.cl_count = pl.nc;
+    rc = encode_maps<C::RG>(a, qw[r], qz[r], sc[r], &E.qw[r], &E.sc[r], &E.qz[r], &E.x[r]);
+    if (rc) return rc;
+    E.p[r] = a;
+    E.ar[r] = views[r];
+  }
+  auto kern = pl.cs > 0 ? w4c_kernel_emu<GP> : w4_kernel_emu<GP>;
+  const int smem = pl.cs > 0 ? CfgC<GP>::kSmem : C::kSmem;
+  B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  if (pl.cs > 8)
+    B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(pl.cs > 0 ? pl.nc * pl.cs : pl.sk.ctas), (unsigned)R);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)pl.cs;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pl.cs > 0 ? 2 : 1;
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, E));
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+
+int launch_w4_allreduce_emulated(b2_nvar* const* handles, int R, const void* const* a,
+                                 const void* const* qw, const void* const* qz,
+                                 const void* const* sc, void* const* residual,
+                                 const void* const* nw, float eps, void* const* y, int M, int K,
+                                 int N, int G, void* const* ws, size_t ws_bytes,
+                                 cudaStream_t stream) {
+  if (R < 1 || R > kEmuMaxRanks)
+    return fail(B2_ERR_INVALID_ARG, "w4_allreduce_emulated: %d ranks (1..%d)", R, kEmuMaxRanks);
+  if (!handles || !a || !qw || !qz || !sc || !y || !ws)
+    return fail(B2_ERR_INVALID_ARG, "w4_allreduce_emulated: null array");
+  if ((residual == nullptr) != (nw == nullptr))
+    return fail(B2_ERR_INVALID_ARG, "w4_allreduce_emulated: residual and norm_weight go together");
+  W4Args args[kEmuMaxRanks];
+  ArView views[kEmuMaxRanks];
+  for (int r = 0; r < R; ++r) {
+    const int rc = fused_args(handles[r], a[r], qw[r], qz[r], sc[r], y[r], M, K, N, G, ws[r],
+                              ws_bytes, residual ? residual[r] : nullptr, nw ? nw[r] : nullptr,
+                              eps, &args[r], &views[r]);
+    if (rc) return rc;
+    if (views[r].rank != r || views[r].world != R)
+      return fail(B2_ERR_STATE, "w4_allreduce_emulated: handle %d is rank %d of %d", r,
+                  views[r].rank, views[r].world);
+    if (args[r].ll != args[0].ll)
+      return fail(B2_ERR_STATE, "w4_allreduce_emulated: the handles' slots differ in size");
+  }
+  switch (G) {
+    case 32: return launch_emu<1>(args, views, qw, qz, sc, R, stream);
+    case 64: return launch_emu<2>(args, views, qw, qz, sc, R, stream);
+    default: return launch_emu<4>(args, views, qw, qz, sc, R, stream);
+  }
 }
 
 }  // namespace b2
@@ -1611,6 +1780,19 @@ extern "C" int b2_w4_gemm_allreduce_rmsnorm(b2_nvar* ar, const void* a, const vo
     return b2::fail(B2_ERR_INVALID_ARG, "w4_allreduce_rmsnorm: null residual or norm_weight");
   return b2::launch_w4_allreduce(ar, a, qw, qz, sc, y, M, K, N, group_size, ws, ws_bytes,
                                  static_cast<cudaStream_t>(stream), residual, norm_weight, eps);
+}
+
+// Ranks of one group emulated on one GPU in one cooperative launch; see include/b2_skinny.h.
+extern "C" int b2_w4_gemm_allreduce_emulated(b2_nvar* const* handles, int ranks,
+                                             const void* const* a, const void* const* qw,
+                                             const void* const* qz, const void* const* sc,
+                                             void* const* residual, const void* const* norm_weight,
+                                             float eps, void* const* y, int M, int K, int N,
+                                             int group_size, void* const* ws, size_t ws_bytes,
+                                             void* stream) {
+  return b2::launch_w4_allreduce_emulated(handles, ranks, a, qw, qz, sc, residual, norm_weight,
+                                          eps, y, M, K, N, group_size, ws, ws_bytes,
+                                          static_cast<cudaStream_t>(stream));
 }
 
 // The W4A16 GEMM without a caller-supplied workspace; see include/b2_skinny.h.
