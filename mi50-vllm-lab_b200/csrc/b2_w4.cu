@@ -824,12 +824,17 @@ struct CfgC {
   static constexpr int kXOff = kStages * kQwStage;
   static constexpr int kScOff = kXOff + kStages * kXBytes;
   static constexpr int kQzOff = kScOff + kStages * kScStride;
-  static constexpr int kRedOff = kQzOff + kStages * kQzStride;  // [8 rows][128 columns] fp32
-  static constexpr int kBarOff = kRedOff + kMaxM * kTileN * 4;
-  static constexpr int kNormOff = align128(kBarOff + (2 * kStages + 2) * 8 + 32);
+  // reduction buffers: my partial tile arranged by destination CTA ([8 rows][W_r] fp32 per CTA
+  // r), and the CS slices the cluster sends me ([CS][8 rows][W] fp32, W <= 128 / CS + 1)
+  static constexpr int kSendOff = kQzOff + kStages * kQzStride;
+  static constexpr int kRecvOff = kSendOff + kMaxM * kTileN * 4;
+  static constexpr int kRecvBytes = kMaxM * (kTileN + 16) * 4;
+  static constexpr int kBarOff = kRecvOff + kRecvBytes;
+  static constexpr int kNormOff = align128(kBarOff + (2 * kStages + 3) * 8 + 32);
   static constexpr int kSmem = 1024 + kNormOff + kNormFloats * 4;
   static_assert(kXOff % 1024 == 0 && kXBytes % 1024 == 0, "swizzled boxes need 1024 B");
-  static_assert(kScOff % 128 == 0 && kQzOff % 128 == 0 && kRedOff % 128 == 0, "alignment");
+  static_assert(kScOff % 128 == 0 && kQzOff % 128 == 0 && kSendOff % 128 == 0 &&
+                    kRecvOff % 128 == 0, "alignment");
 };
 
 template <int GP, bool FUSED>
@@ -845,12 +850,14 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
   uint8_t* s_x = smem + C::kXOff;
   uint8_t* s_sc = smem + C::kScOff;
   uint8_t* s_qz = smem + C::kQzOff;
-  float* s_red = reinterpret_cast<float*>(smem + C::kRedOff);
+  float* s_send = reinterpret_cast<float*>(smem + C::kSendOff);
+  const float* s_recv = reinterpret_cast<const float*>(smem + C::kRecvOff);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* empty = full + kStages;
-  uint64_t* red_full = empty + kStages;  // every CTA of the cluster left its partial tile
-  uint64_t* red_empty = red_full + 1;    // every CTA of the cluster finished reading mine
-  volatile int* s_abort = reinterpret_cast<volatile int*>(red_empty + 1);
+  uint64_t* red_full = empty + kStages;  // the CS slices of the tile have landed in s_recv
+  uint64_t* red_empty = red_full + 1;    // every receiver has added up my previous tile
+  uint64_t* pub_bar = red_empty + 1;     // (CTA 0, fp32 flag exchange) every CTA pushed its slice
+  volatile int* s_abort = reinterpret_cast<volatile int*>(pub_bar + 1);
   volatile int* s_flag = s_abort + 1;
   volatile uint32_t* s_gen = reinterpret_cast<volatile uint32_t*>(s_abort + 2);
 
@@ -868,8 +875,9 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kWarps);
     }
-    mbar_init(red_full, CS);
+    mbar_init(red_full, 1);  // my own expect-tx; the senders' copies complete the bytes
     mbar_init(red_empty, CS);
+    mbar_init(pub_bar, CS);
     *s_abort = 0;
     *s_flag = 0;
     mbar_fence_init();
@@ -954,7 +962,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
   const int tid = threadIdx.x;
   // column slice of every tile that this CTA reduces and writes
   const int c0 = kTileN * crank / CS, c1 = kTileN * (crank + 1) / CS, W = c1 - c0;
-  const uint32_t red_addr = smem_u32(s_red);
+  const uint32_t send_addr = smem_u32(s_send), recv_addr = smem_u32(s_recv);
   const uint32_t x_base0 = smem_u32(s_x), qw_base0 = smem_u32(s_qw + warp * kQwBox);
 
   float acc[2][4];
@@ -981,39 +989,62 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
     }
 
     // ---------------------------------------------------------------- tile epilogue: reduce
-    // my partial tile -> my reduction buffer, once every CTA has read the previous one. One
-    // thread waits; the CTA barrier orders the other threads after its acquire (and, further
-    // down, their writes before its release-arrive), as the PTX memory model's causality order
-    // composes the two.
+    // Push, not pull: every CTA writes its partial tile into its send buffer arranged by the CTA
+    // that owns each column slice, and sends slice r to CTA r with one bulk copy (shared::cta ->
+    // shared::cluster) that completes its bytes on CTA r's red_full. A CTA then adds the CS
+    // slices it received in cluster rank order from its own shared memory. With one tile per
+    // CTA there is no round trip at all; with more, the next tile's copies wait until every
+    // receiver has added up the previous one (red_empty).
+    // (a) the send buffer: the copies that read it for the previous tile must be done reading
     if (it > 0) {
-      if (tid == 0) *s_flag = mbar_wait_cluster(red_empty, (uint32_t)((it - 1) & 1), s_abort);
+      if (tid < CS) bulk_wait_read_all();
       named_bar_sync(1, kWarps * 32);
-      ok = ok && *s_flag;
     }
     {
-      const float4 v0 = make_float4(acc[0][0], acc[0][2], acc[1][0], acc[1][2]);  // m = 2t
-      const float4 v1 = make_float4(acc[0][1], acc[0][3], acc[1][1], acc[1][3]);  // m = 2t + 1
-      if (2 * t < p.M) *reinterpret_cast<float4*>(s_red + (2 * t) * kTileN + colw) = v0;
-      if (2 * t + 1 < p.M) *reinterpret_cast<float4*>(s_red + (2 * t + 1) * kTileN + colw) = v1;
+      const float v[2][4] = {{acc[0][0], acc[0][2], acc[1][0], acc[1][2]},   // row 2t
+                             {acc[0][1], acc[0][3], acc[1][1], acc[1][3]}};  // row 2t + 1
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = colw + j;
+        const int r = ((col + 1) * CS - 1) / kTileN;  // the CTA whose slice holds col
+        const int cr0 = kTileN * r / CS, wr = kTileN * (r + 1) / CS - cr0;
+        float* dst = s_send + kMaxM * cr0 + (col - cr0);
+        dst[(2 * t) * wr] = v[0][j];
+        dst[(2 * t + 1) * wr] = v[1][j];
+      }
     }
 #pragma unroll
     for (int T = 0; T < 2; ++T)
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[T][i] = 0.f;
+    fence_proxy_async_smem();  // these generic writes precede the copies' (async proxy) reads
     named_bar_sync(1, kWarps * 32);
-    // lane q tells CTA q (one release-arrive each, issued together by warp 0)
-    if (tid < CS) mbar_arrive_remote(mapa_shared(smem_u32(red_full), (uint32_t)tid));
-    if (tid == 0) *s_flag = mbar_wait_cluster(red_full, (uint32_t)(it & 1), s_abort);
+    // (b) lane r of warp 0 sends slice r into CTA r's receive buffer, at my rank's place
+    if (tid < CS) {
+      const bool go = it == 0 || mbar_wait_cluster(red_empty, (uint32_t)((it - 1) & 1), s_abort);
+      if (go) {
+        const int cr0 = kTileN * tid / CS, wr = kTileN * (tid + 1) / CS - cr0;
+        const uint32_t bytes = (uint32_t)(kMaxM * wr * 4);
+        bulk_copy_to_peer(mapa_shared(recv_addr + (uint32_t)crank * bytes, (uint32_t)tid),
+                          send_addr + (uint32_t)(kMaxM * cr0 * 4), bytes,
+                          mapa_shared(smem_u32(red_full), (uint32_t)tid));
+        bulk_commit();
+      }
+    }
+    // (c) my slice from every CTA of the cluster
+    if (tid == 0) {
+      mbar_arrive_expect_tx(red_full, (uint32_t)(CS * kMaxM * W * 4));
+      *s_flag = mbar_wait_cluster(red_full, (uint32_t)(it & 1), s_abort);
+    }
     named_bar_sync(1, kWarps * 32);
     ok = ok && *s_flag;
     // slice [c0, c1) of the tile: the CS partials added in rank order
     for (int idx = tid; idx < p.M * W; idx += kWarps * 32) {
       const int m = idx / W, col = c0 + (idx - m * W);
-      const uint32_t off = red_addr + (uint32_t)(m * kTileN + col) * 4u;
-      float part[16];  // all CS loads in flight, then the sum in rank order
+      const float* src = s_recv + idx;  // [q][8 rows][W]: element (m, col) of sender q
+      float part[16];
 #pragma unroll
-      for (int q = 0; q < 16; ++q)
-        part[q] = (q < CS) ? ld_dsmem_f32(mapa_shared(off, (uint32_t)q)) : 0.f;
+      for (int q = 0; q < 16; ++q) part[q] = (q < CS) ? src[q * kMaxM * W] : 0.f;
       float s = 0.f;
 #pragma unroll
       for (int q = 0; q < 16; ++q)
@@ -1040,13 +1071,21 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
         }
       }
     }
-    named_bar_sync(1, kWarps * 32);
-    if (tid < CS) mbar_arrive_remote(mapa_shared(smem_u32(red_empty), (uint32_t)tid));
-    // Every CTA of the cluster has pushed its slice once CTA 0's buffer release completes: CTA 0
-    // publishes the tile with one system-scope fence (the peers' pushes happen before it through
-    // their CTA barrier and cluster-scope release, which the fence's cumulativity covers).
-    if (FUSED && !p.ll && crank == 0 && tid == 0) {
-      if (mbar_wait_cluster(red_empty, (uint32_t)(it & 1), s_abort)) ar_publish(ar, tile, e);
+    // (d) tell every sender that my receive buffer is free again (only if it will be reused)
+    if (it + 1 < ntile) {
+      fence_proxy_async_smem();  // my reads precede the next copies into the buffer
+      named_bar_sync(1, kWarps * 32);
+      if (tid < CS) mbar_arrive_remote(mapa_shared(smem_u32(red_empty), (uint32_t)tid));
+    }
+    // fp32 flag exchange: every CTA of the cluster has pushed its slice once CTA 0's pub_bar
+    // completes; CTA 0 then publishes the tile with one system-scope fence (the peers' pushes
+    // happen before it through their CTA barrier and cluster-scope release, which the fence's
+    // cumulativity covers).
+    if (FUSED && !p.ll) {
+      named_bar_sync(1, kWarps * 32);
+      if (tid == 0) mbar_arrive_remote(mapa_shared(smem_u32(pub_bar), 0u));
+      if (crank == 0 && tid == 0 && mbar_wait_cluster(pub_bar, (uint32_t)(it & 1), s_abort))
+        ar_publish(ar, tile, e);
     }
   }
   if constexpr (FUSED) {
@@ -1141,19 +1180,24 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
     named_bar_sync(1, kWarps * 32);
     if (tid == 0) ar_finish(ar, e);
   }
-  // Nobody may still read my reduction buffer or arrive on my barriers when this CTA exits: the
-  // release of my last tile's buffer is every peer's last access to my shared memory.
+  // Before this CTA exits, no peer may still write into its shared memory or arrive on its
+  // barriers, and its own outgoing copies must be done reading its send buffer. On the normal
+  // path every such access was waited for above; after a wait gave up, wait for the last ones
+  // again with the full bound (exiting under a peer's copy is worse than waiting).
   {
-    // wait the full bound here even after an earlier timeout: exiting while a peer still reads
-    // this CTA's shared memory is worse than waiting
     volatile int* no_abort = s_flag + 2;  // a zeroed word of its own
     named_bar_sync(1, kWarps * 32);
-    if (tid == 0) {
+    if (tid == 0 && *s_abort) {
       *no_abort = 0;
-      if (!mbar_wait_cluster(red_empty, (uint32_t)((ntile - 1) & 1), no_abort)) *s_flag = 0;
+      mbar_wait_cluster(red_full, (uint32_t)((ntile - 1) & 1), no_abort);
+      *no_abort = 0;
+      if (ntile > 1) mbar_wait_cluster(red_empty, (uint32_t)((ntile - 2) & 1), no_abort);
+      *no_abort = 0;
+      if (FUSED && !p.ll && crank == 0)
+        mbar_wait_cluster(pub_bar, (uint32_t)((ntile - 1) & 1), no_abort);
     }
+    if (tid < CS) bulk_wait_read_all();
     named_bar_sync(1, kWarps * 32);
-    ok = ok && *s_flag;
   }
   if (!ok && lane == 0) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
 }

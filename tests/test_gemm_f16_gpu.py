@@ -45,6 +45,30 @@ def test_config1_lm_head_sampled_columns(ops):
     del w
 
 
+# The drafter layers the reference times (kernels/bench_skinny.py:34-37), as (N, K), at its row
+# counts (kernels/bench_skinny.py:12: 1, 3, 4, 7, 8).
+DRAFTER = {"dr_qkv": (3072, 5120), "dr_o": (5120, 2048), "dr_gate_up": (17408, 5120),
+           "dr_down": (5120, 8704), "dr_fc": (5120, 25600), "dr_ctx_kv": (5120, 5120),
+           "dr_kproj": (1280, 5120)}
+
+
+@pytest.mark.parametrize("M", [1, 3, 4, 7, 8])
+@pytest.mark.parametrize("layer", list(DRAFTER))
+def test_drafter_shapes(ops, layer, M):
+    """Every drafter shape of the reference's fp16 benchmark, with its weights N(0, 0.02) and
+    activations N(0, 1) (kernels/bench_skinny.py:41-43), checked on sampled columns against the
+    float64 oracle, and deterministic."""
+    N, K = DRAFTER[layer]
+    g = torch.Generator(device="cuda").manual_seed(N + K + M)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
+    y = ops.gemm(x, w, 20)
+    assert y.shape == (M, N) and torch.isfinite(y).all()
+    cols = sample_columns(N, 400, seed=M)
+    check(y[:, torch.from_numpy(cols).cuda()], f16_ref_sampled(x, w, cols), f"{layer} M={M}")
+    assert torch.equal(y, ops.gemm(x, w, 20)), "not deterministic"
+
+
 def test_weights_written_by_the_previous_kernel(ops):
     """Weights produced by the kernel launched just before the GEMM (no host sync in between)
     are read in full: the early start of the GEMM's CTAs must not read them before that
