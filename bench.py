@@ -343,24 +343,36 @@ def measure_gemm(lib, capi, ws, name, kind, M, K, N, G, steps, warmup, peak, l2)
     to exceed 3x L2 (so every launch reads HBM), timed by replaying the graph."""
     import torch
 
-    wbytes = K * N // 2 if kind == "w4" else 2 * N * K
-    nb = w4_bytes(M, K, N, G) if kind == "w4" else f16_bytes(M, K, N)
+    w4 = kind in ("w4", "w4p")
+    wbytes = K * N // 2 if w4 else 2 * N * K
+    nb = w4_bytes(M, K, N, G) if w4 else f16_bytes(M, K, N)
     copies = max(1, int(3 * l2 // wbytes) + 1)
     g = torch.Generator(device="cuda").manual_seed(M * K + N)
     x = torch.randn(M, K, device="cuda", generator=g).half()
     y = torch.empty(M, N, dtype=torch.float16, device="cuda")
     calls = []
     for _ in range(copies):
-        if kind == "w4":
+        if w4:
             qw = torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32, generator=g)
             qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda", dtype=torch.int32, generator=g)
             sc = (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half()
-            calls.append((qw, qz, sc))
+            if kind == "w4p":  # repacked once, as at weight-load time; the originals are freed
+                pk = torch.empty(lib.b2_w4_packed_bytes(K, N, G), dtype=torch.uint8, device="cuda")
+                capi.check(lib.b2_w4_repack(qw.data_ptr(), qz.data_ptr(), sc.data_ptr(), K, N, G,
+                                            pk.data_ptr(), pk.numel(), 0), "b2_w4_repack")
+                torch.cuda.synchronize()
+                calls.append((pk,))
+                del qw, qz, sc
+            else:
+                calls.append((qw, qz, sc))
         else:
             calls.append((torch.randn(N, K, device="cuda", generator=g) * 0.02).half(),)
 
     def launch(t, sp):
-        if kind == "w4":
+        if kind == "w4p":
+            rc = lib.b2_w4_gemm_packed(x.data_ptr(), t[0].data_ptr(), y.data_ptr(), M, K, N, G,
+                                       ws.data_ptr(), ws.numel(), sp)
+        elif kind == "w4":
             qw, qz, sc = t
             rc = lib.b2_w4_gemm(x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(),
                                 y.data_ptr(), M, K, N, G, ws.data_ptr(), ws.numel(), sp)
@@ -636,6 +648,13 @@ SWEEP = (
     + [(f"drafter_{nm}_M{M}", "f16", M, K, N, 0) for M in (1, 7, 8)
        for nm, (N, K) in DRAFTER.items()]
     + [("check_w4_G32", "w4", 8, 5120, 1024, 32)]
+    # weights repacked at load time (b2_w4_repack): the same shapes through b2_w4_gemm_packed
+    + [("cfg0_packed", "w4p", 7, 4096, 4096, 128)]
+    + [(f"cfg2_{nm}_M8_packed", "w4p", 8, K, N, 128)
+       for nm, (K, N) in {"qkv": (5120, 8192), "o_proj": (6144, 5120), "gate_up": (5120, 34816),
+                          "down": (17408, 5120)}.items()]
+    + [(f"cfg3_down_TP{P}_packed", "w4p", 8, 17408 // P, 5120, 128) for P in (2, 4, 8)]
+    + [(f"cfg4_TP8_{nm}_packed", "w4p", 8, K, N, 128) for nm, (K, N) in layer_shapes(8).items()]
 )
 # Extra cases for --profile only: the lm_head kernel on a 335 MB slice (above L2, small enough
 # for a multi-pass ncu capture); traffic scales with N for this kernel.
@@ -666,7 +685,7 @@ def run_sweep(args):
         if args.only and not any(o in w[0] for o in args.only.split(",")):
             continue
         r = measure_gemm(lib, capi, ws, *w, args.steps, args.warmup, peak, l2)
-        if w[1] == "w4":
+        if w[1] in ("w4", "w4p"):
             r["plan"] = capi.w4_plan(w[2], w[3], w[4], w[5])
         print(json.dumps(r), flush=True)
         torch.cuda.empty_cache()

@@ -115,6 +115,26 @@ int b2_w4_gemm(const void* a, const void* qw, const void* qz, const void* sc, vo
                int K, int N, int group_size, void* ws, size_t ws_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------------
+ * W4A16 with weights repacked once at load time
+ *
+ * The reference's loader converts GPTQ checkpoints once, before the first forward
+ * (gptq_shuffle at weight-load time); b2_w4_repack is the B200 step that may follow it. It
+ * rewrites qw, qz and sc into one buffer in which each 128-column x 128-k unit is a single
+ * contiguous run of bytes (its weights in the order the kernels' shared memory holds them, then
+ * its scale and zero rows), so a unit is one sequential read from HBM instead of 16 rows of 512 B
+ * set N * 4 bytes apart. The product is bit-identical to b2_w4_gemm on the original tensors.
+ *   b2_w4_packed_bytes : size of the buffer (0 when K, N, G break b2_w4_gemm's contract).
+ *   b2_w4_repack       : qw, qz, sc as for b2_w4_gemm -> out (16-byte aligned, >= that size).
+ *                        Asynchronous on `stream`; the inputs may be freed once it completes.
+ *   b2_w4_gemm_packed  : b2_w4_gemm with the repacked buffer in place of qw, qz, sc.
+ * ---------------------------------------------------------------------------------------- */
+size_t b2_w4_packed_bytes(int K, int N, int group_size);
+int b2_w4_repack(const void* qw, const void* qz, const void* sc, int K, int N, int group_size,
+                 void* out, size_t out_bytes, void* stream);
+int b2_w4_gemm_packed(const void* a, const void* packed, void* y, int M, int K, int N,
+                      int group_size, void* ws, size_t ws_bytes, void* stream);
+
+/* ------------------------------------------------------------------------------------------
  * W4A16 skinny GEMM that allocates nothing (no counterpart in the reference)
  *
  * Same operands, layouts, contract and results as b2_w4_gemm, but without the workspace

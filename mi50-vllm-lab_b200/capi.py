@@ -44,6 +44,9 @@ _SIGS = {
     "b2_workspace_status": (_i, [_vp, _i, C.POINTER(_i)]),
     "b2_gemm_f16": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     "b2_w4_gemm": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "b2_w4_packed_bytes": (_sz, [_i, _i, _i]),
+    "b2_w4_repack": (_i, [_vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
+    "b2_w4_gemm_packed": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "b2_w4_gemm_noalloc": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "b2_w4_noalloc_scratch": (_i, [C.POINTER(_vp), C.POINTER(_sz)]),
     "b2_registry_open": (_i, [C.c_char_p, _i, _i, C.POINTER(_vp)]),

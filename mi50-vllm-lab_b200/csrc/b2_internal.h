@@ -35,6 +35,10 @@ int device_info(DeviceInfo* out);
 int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
               uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
               CUtensorMapSwizzle swizzle);
+// Encode a 3-D tiled tensor map. dims/box innermost first; strides (bytes) of dims 1 and 2, in
+// any order of size (a middle dimension may step further than the outer one).
+int encode_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
+              const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle);
 
 // Workspace layout: [status words][tile counters][partial slots][row sums of the fused RMSNorm,
 // kMaxM floats per CTA].

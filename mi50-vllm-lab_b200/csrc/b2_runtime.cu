@@ -80,13 +80,18 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 namespace {
 struct MapKey {
   const void* base;
-  uint64_t inner, outer, stride;
-  uint32_t box_inner, box_outer;
+  int rank;
+  uint64_t dims[3], strides[2];
+  uint32_t box[3];
   int dtype, swizzle, device;
   bool operator==(const MapKey& o) const {
-    return base == o.base && inner == o.inner && outer == o.outer && stride == o.stride &&
-           box_inner == o.box_inner && box_outer == o.box_outer && dtype == o.dtype &&
-           swizzle == o.swizzle && device == o.device;
+    if (base != o.base || rank != o.rank || dtype != o.dtype || swizzle != o.swizzle ||
+        device != o.device)
+      return false;
+    for (int i = 0; i < rank; ++i)
+      if (dims[i] != o.dims[i] || box[i] != o.box[i] || (i + 1 < rank && strides[i] != o.strides[i]))
+        return false;
+    return true;
   }
 };
 struct MapEntry {
@@ -99,32 +104,47 @@ thread_local MapEntry t_maps[kMapCache];
 
 size_t map_hash(const MapKey& k) {
   size_t h = reinterpret_cast<uintptr_t>(k.base) >> 4;
-  h = h * 1000003u ^ (size_t)k.inner;
-  h = h * 1000003u ^ (size_t)k.outer;
-  h = h * 1000003u ^ ((size_t)k.box_inner << 8 | k.box_outer);
-  h = h * 1000003u ^ (size_t)(k.dtype * 31 + k.swizzle * 7 + k.device);
+  for (int i = 0; i < k.rank; ++i) {
+    h = h * 1000003u ^ (size_t)k.dims[i];
+    h = h * 1000003u ^ (size_t)k.box[i];
+    if (i + 1 < k.rank) h = h * 1000003u ^ (size_t)k.strides[i];
+  }
+  h = h * 1000003u ^ (size_t)(k.dtype * 31 + k.swizzle * 7 + k.device + k.rank * 131);
   return h;
 }
-}  // namespace
 
-int encode_2d_uncached(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
-                       uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
-                       uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+int encode_uncached(CUtensorMap* map, const MapKey& k) {
+  auto fn = get_encode_fn();
+  if (!fn) return fail(B2_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {0, 0, 0}, strides[2] = {0, 0};
+  cuuint32_t box[3] = {0, 0, 0}, estr[3] = {1, 1, 1};
+  for (int i = 0; i < k.rank; ++i) {
+    dims[i] = k.dims[i];
+    box[i] = k.box[i];
+    if (i + 1 < k.rank) strides[i] = k.strides[i];
+  }
+  CUresult r = fn(map, (CUtensorMapDataType)k.dtype, (cuuint32_t)k.rank, const_cast<void*>(k.base),
+                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  (CUtensorMapSwizzle)k.swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B2_ERR_INVALID_ARG,
+                "cuTensorMapEncodeTiled failed (%d): rank %d, dims %llu x %llu x %llu, strides "
+                "%llu %llu B, box %u x %u x %u",
+                (int)r, k.rank, (unsigned long long)dims[0], (unsigned long long)dims[1],
+                (unsigned long long)dims[2], (unsigned long long)strides[0],
+                (unsigned long long)strides[1], box[0], box[1], box[2]);
+  return B2_OK;
+}
 
-int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
-              uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
-              CUtensorMapSwizzle swizzle) {
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const MapKey key{base, inner, outer, row_stride_bytes, box_inner, box_outer, (int)dtype,
-                   (int)swizzle, dev};
+int encode_cached(CUtensorMap* map, MapKey key) {
+  cudaGetDevice(&key.device);
   MapEntry& e = t_maps[map_hash(key) % kMapCache];
   if (e.valid && e.key == key) {
     *map = e.map;
     return B2_OK;
   }
-  const int rc = encode_2d_uncached(map, dtype, base, inner, outer, row_stride_bytes, box_inner,
-                                    box_outer, swizzle);
+  const int rc = encode_uncached(map, key);
   if (rc == B2_OK) {
     e.key = key;
     e.map = *map;
@@ -132,25 +152,38 @@ int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uin
   }
   return rc;
 }
+}  // namespace
 
-int encode_2d_uncached(CUtensorMap* map, CUtensorMapDataType dtype, const void* base,
-                       uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
-                       uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
-  auto fn = get_encode_fn();
-  if (!fn) return fail(B2_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_stride_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(B2_ERR_INVALID_ARG,
-                "cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, stride %llu B, box %u x %u",
-                (int)r, (unsigned long long)inner, (unsigned long long)outer,
-                (unsigned long long)row_stride_bytes, box_inner, box_outer);
-  return B2_OK;
+int encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner,
+              uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swizzle) {
+  MapKey k = {};
+  k.base = base;
+  k.rank = 2;
+  k.dims[0] = inner;
+  k.dims[1] = outer;
+  k.strides[0] = row_stride_bytes;
+  k.box[0] = box_inner;
+  k.box[1] = box_outer;
+  k.dtype = (int)dtype;
+  k.swizzle = (int)swizzle;
+  return encode_cached(map, k);
+}
+
+int encode_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
+              const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle) {
+  MapKey k = {};
+  k.base = base;
+  k.rank = 3;
+  for (int i = 0; i < 3; ++i) {
+    k.dims[i] = dims[i];
+    k.box[i] = box[i];
+  }
+  k.strides[0] = strides_bytes[0];
+  k.strides[1] = strides_bytes[1];
+  k.dtype = (int)dtype;
+  k.swizzle = (int)swizzle;
+  return encode_cached(map, k);
 }
 
 // ----------------------------------------------------------------------------------------------

@@ -100,7 +100,17 @@ struct W4Args {
   const __half* nw;  // [N] norm weight
   __half* res;       // [M, N] residual: read, then overwritten with the sum
   float* npart;      // [grid][kMaxM] per-CTA sums of squares (workspace)
+  // weights repacked at load time (b2_w4_repack), or null: unit (tile, ku) is pk_unit contiguous
+  // bytes at pk + (tile * K / 128 + ku) * pk_unit holding exactly the stage's shared-memory image:
+  // its qw block (8 KB, already swizzled), then its scale rows, then its zero rows
+  const uint8_t* pk;
+  int pk_unit;
 };
+
+// The repacked bytes of unit (tile, ku).
+__device__ __forceinline__ const uint8_t* packed_unit(const W4Args& p, int tile, int ku) {
+  return p.pk + ((size_t)tile * (size_t)(p.K / kUnitK) + (size_t)ku) * (size_t)p.pk_unit;
+}
 
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;  // (a & b) | c
@@ -523,9 +533,11 @@ __device__ __forceinline__ void w4_body(const CUtensorMap& tm_qw, const CUtensor
   // ------------------------------------------------------------------ producer warp (1 thread)
   if (warp == kWarps) {
     if (lane == 0) {
-      tma_prefetch_desc(&tm_qw);
-      tma_prefetch_desc(&tm_sc);
-      tma_prefetch_desc(&tm_qz);
+      if (!p.pk) {
+        tma_prefetch_desc(&tm_qw);
+        tma_prefetch_desc(&tm_sc);
+        tma_prefetch_desc(&tm_qz);
+      }
       tma_prefetch_desc(&tm_x);
       const uint64_t pol_w = l2_evict_first_policy();   // weights: read once
       const uint64_t pol_x = l2_evict_normal_policy();  // activations: read by every CTA
@@ -533,16 +545,20 @@ __device__ __forceinline__ void w4_body(const CUtensorMap& tm_qw, const CUtensor
         const int n0 = c.tile * kTileN;
         const int grow = (c.ku * kUnitK) / p.G;
         mbar_arrive_expect_tx(&full[st], C::kTx);
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w)
-          tma_load_2d(s_qw + st * kQwStage + w * kQwBox, &tm_qw, &full[st], n0 + 32 * w,
-                      c.ku * 16, pol_w);
+        if (p.pk) {
+          const uint8_t* u = packed_unit(p, c.tile, c.ku);
+          bulk_load(s_qw + st * kQwStage, u, kQwStage, &full[st], pol_w);
+          bulk_load(s_sc + st * C::kScStride, u + kQwStage, C::kScBytes, &full[st], pol_w);
+          bulk_load(s_qz + st * C::kQzStride, u + kQwStage + C::kScBytes, C::kQzBytes, &full[st],
+                    pol_w);
+          return;
+        }
+        tma_load_3d(s_qw + st * kQwStage, &tm_qw, &full[st], 0, c.ku * 16, n0 / 32, pol_w);
         tma_load_2d(s_sc + st * C::kScStride, &tm_sc, &full[st], n0, grow, pol_w);
         tma_load_2d(s_qz + st * C::kQzStride, &tm_qz, &full[st], n0 / 8, grow, pol_w);
       };
       auto issue_x = [&](int st, const UnitCursor& c) {
-        tma_load_2d(s_x + st * C::kXBytes, &tm_x, &full[st], c.ku * kUnitK, 0, pol_x);
-        tma_load_2d(s_x + st * C::kXBytes + 1024, &tm_x, &full[st], c.ku * kUnitK + 64, 0, pol_x);
+        tma_load_3d(s_x + st * C::kXBytes, &tm_x, &full[st], 0, 0, c.ku * 2, pol_x);
       };
       // Until the previous grid on the stream has completed, its stores may not be visible:
       // only warm L2 with the first stages' weights, then wait, then load.
@@ -551,8 +567,11 @@ __device__ __forceinline__ void w4_body(const CUtensorMap& tm_qw, const CUtensor
         UnitCursor cp = c0;
         for (int j = 0; j < kStages && cp.left > 0; ++j, cp.next(sk)) {
           const int n0 = cp.tile * kTileN, grow = (cp.ku * kUnitK) / p.G;
-#pragma unroll
-          for (int w = 0; w < kWarps; ++w) tma_prefetch_l2_2d(&tm_qw, n0 + 32 * w, cp.ku * 16);
+          if (p.pk) {
+            bulk_prefetch_l2(packed_unit(p, cp.tile, cp.ku), (uint32_t)p.pk_unit);
+            continue;
+          }
+          tma_prefetch_l2_3d(&tm_qw, 0, cp.ku * 16, n0 / 32);
           tma_prefetch_l2_2d(&tm_sc, n0, grow);
           tma_prefetch_l2_2d(&tm_qz, n0 / 8, grow);
         }
@@ -889,9 +908,11 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
   // ------------------------------------------------------------------ producer warp (1 thread)
   if (warp == kWarps) {
     if (lane == 0) {
-      tma_prefetch_desc(&tm_qw);
-      tma_prefetch_desc(&tm_sc);
-      tma_prefetch_desc(&tm_qz);
+      if (!p.pk) {
+        tma_prefetch_desc(&tm_qw);
+        tma_prefetch_desc(&tm_sc);
+        tma_prefetch_desc(&tm_qz);
+      }
       tma_prefetch_desc(&tm_x);
       const uint64_t pol_w = l2_evict_first_policy();
       const uint64_t pol_x = l2_evict_normal_policy();
@@ -908,16 +929,20 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
         if (with_w) {
           const int grow = (ku * kUnitK) / p.G;
           mbar_arrive_expect_tx(&full[st], C::kTx);
-#pragma unroll
-          for (int w = 0; w < kWarps; ++w)
-            tma_load_2d(s_qw + st * kQwStage + w * kQwBox, &tm_qw, &full[st], n0 + 32 * w, ku * 16,
-                        pol_w);
-          tma_load_2d(s_sc + st * C::kScStride, &tm_sc, &full[st], n0, grow, pol_w);
-          tma_load_2d(s_qz + st * C::kQzStride, &tm_qz, &full[st], n0 / 8, grow, pol_w);
+          if (p.pk) {
+            const uint8_t* u = packed_unit(p, tile, ku);
+            bulk_load(s_qw + st * kQwStage, u, kQwStage, &full[st], pol_w);
+            bulk_load(s_sc + st * C::kScStride, u + kQwStage, C::kScBytes, &full[st], pol_w);
+            bulk_load(s_qz + st * C::kQzStride, u + kQwStage + C::kScBytes, C::kQzBytes,
+                      &full[st], pol_w);
+          } else {
+            tma_load_3d(s_qw + st * kQwStage, &tm_qw, &full[st], 0, ku * 16, n0 / 32, pol_w);
+            tma_load_2d(s_sc + st * C::kScStride, &tm_sc, &full[st], n0, grow, pol_w);
+            tma_load_2d(s_qz + st * C::kQzStride, &tm_qz, &full[st], n0 / 8, grow, pol_w);
+          }
         }
         if (with_x) {
-          tma_load_2d(s_x + st * C::kXBytes, &tm_x, &full[st], ku * kUnitK, 0, pol_x);
-          tma_load_2d(s_x + st * C::kXBytes + 1024, &tm_x, &full[st], ku * kUnitK + 64, 0, pol_x);
+          tma_load_3d(s_x + st * C::kXBytes, &tm_x, &full[st], 0, 0, ku * 2, pol_x);
         }
       };
       // until the previous grid has completed only warm L2 with the first stages' weights
@@ -925,8 +950,11 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
         int tile, ku;
         where(j, tile, ku);
         const int n0 = tile * kTileN, grow = (ku * kUnitK) / p.G;
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) tma_prefetch_l2_2d(&tm_qw, n0 + 32 * w, ku * 16);
+        if (p.pk) {
+          bulk_prefetch_l2(packed_unit(p, tile, ku), (uint32_t)p.pk_unit);
+          continue;
+        }
+        tma_prefetch_l2_3d(&tm_qw, 0, ku * 16, n0 / 32);
         tma_prefetch_l2_2d(&tm_sc, n0, grow);
         tma_prefetch_l2_2d(&tm_qz, n0 / 8, grow);
       }
@@ -1246,18 +1274,34 @@ template <int RG>
 int encode_maps(const W4Args& a, const void* qw, const void* qz, const void* sc, CUtensorMap* m_qw,
                 CUtensorMap* m_sc, CUtensorMap* m_qz, CUtensorMap* m_x) {
   const int K = a.K, N = a.N, G = a.G;
-  int rc = encode_2d(m_qw, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, (uint64_t)N, (uint64_t)(K / 8),
-                     (uint64_t)N * 4, 32, 16, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  rc = encode_2d(m_sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, (uint64_t)N, (uint64_t)(K / G),
-                 (uint64_t)N * 2, kTileN, RG, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc) return rc;
-  rc = encode_2d(m_qz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, (uint64_t)(N / 8), (uint64_t)(K / G),
-                 (uint64_t)N / 2, kTileN / 8, RG, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (rc) return rc;
-  // activations [M rows, K] fp16; rows M..7 of a box read as zeros (out of bounds)
-  return encode_2d(m_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, (uint64_t)K, (uint64_t)a.M,
-                   (uint64_t)K * 2, 64, kMaxM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (a.pk) {  // repacked weights come in by plain bulk copies: no weight maps (left zeroed)
+    std::memset(m_qw, 0, sizeof(CUtensorMap));
+    std::memset(m_sc, 0, sizeof(CUtensorMap));
+    std::memset(m_qz, 0, sizeof(CUtensorMap));
+  } else {
+    // qw [K/8 word rows, N] int32 as (32 columns, word rows, 32-column blocks): one box is a
+    // unit's 4 blocks x 16 rows, laid out [block][row][32 words] with each 128-byte row swizzled
+    // by its row index, as 4 separate 32 x 16 boxes would be (N % 32 == 0: whole blocks)
+    const uint64_t qd[3] = {32, (uint64_t)(K / 8), (uint64_t)(N / 32)};
+    const uint64_t qs[2] = {(uint64_t)N * 4, 128};
+    const uint32_t qb[3] = {32, 16, (uint32_t)kWarps};
+    int rc = encode_3d(m_qw, CU_TENSOR_MAP_DATA_TYPE_INT32, qw, qd, qs, qb,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = encode_2d(m_sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, sc, (uint64_t)N, (uint64_t)(K / G),
+                   (uint64_t)N * 2, kTileN, RG, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = encode_2d(m_qz, CU_TENSOR_MAP_DATA_TYPE_INT32, qz, (uint64_t)(N / 8), (uint64_t)(K / G),
+                   (uint64_t)N / 2, kTileN / 8, RG, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  // activations [M rows, K] fp16 as (64 k, rows, 64-k chunks): one box is a unit's two chunks of
+  // 8 rows, [chunk][row][64] (K % 128 == 0); rows M..7 of a box read as zeros (out of bounds)
+  const uint64_t xd[3] = {64, (uint64_t)a.M, (uint64_t)(K / 64)};
+  const uint64_t xs[2] = {(uint64_t)K * 2, 128};
+  const uint32_t xb[3] = {64, kMaxM, 2};
+  return encode_3d(m_x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a.x, xd, xs, xb,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // B2_LOG_PLAN=1 in the environment prints the split-K plan of every W4 launch to stderr.
@@ -1507,6 +1551,8 @@ W4Args make_args(const void* a, void* y, int M, int K, int N, int G, void* ws) {
   r.nw = nullptr;
   r.res = nullptr;
   r.npart = nullptr;
+  r.pk = nullptr;
+  r.pk_unit = 0;
   return r;
 }
 
@@ -1602,6 +1648,58 @@ int noalloc_scratch(cudaStream_t stream, unsigned char** out) {
   return B2_OK;
 }
 
+// ------------------------------------------------------------------------------------------------
+// Weight repack (load time). Unit (tile, ku) becomes unit_bytes contiguous bytes at
+// out + (tile * K / 128 + ku) * unit_bytes: the stage image the kernels' consumers read.
+//   [0, 8192)            qw: block w (32 columns), word row r (k = 8 (16 ku + r) ..), 16-byte
+//                        chunk c (columns 4c..4c+3 of the block) at w * 2048 + r * 128 +
+//                        ((c ^ (r & 7)) << 4): the 128-byte swizzle the tensor copy applies
+//   [8192, +RG * 256)    scales of the unit's RG group rows, 128 fp16 each
+//   [.., +RG * 64)       zeros of those rows, 16 packed words each
+// with RG = 128 / G group rows per unit (1 for G >= 128: the unit's own group row). Columns past
+// N hold zeros (a zero scale: they add nothing). A pure permutation of the bytes the kernels read
+// from the original layout, so the products are bit-identical.
+// ------------------------------------------------------------------------------------------------
+int packed_unit_bytes(int G) {
+  const int RG = G >= kUnitK ? 1 : kUnitK / G;
+  return kQwStage + RG * (kTileN * 2 + (kTileN / 8) * 4);
+}
+
+__global__ void __launch_bounds__(256) w4_repack_kernel(const uint32_t* __restrict__ qw,
+                                                        const uint32_t* __restrict__ qz,
+                                                        const __half* __restrict__ sc,
+                                                        uint8_t* __restrict__ out, int K, int N,
+                                                        int G, int unit_bytes) {
+  const int ku = blockIdx.x, tile = blockIdx.y;
+  const int RG = G >= kUnitK ? 1 : kUnitK / G;
+  const int grow0 = (ku * kUnitK) / G;
+  const int sc_chunks = RG * kTileN * 2 / 16;
+  uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)tile * (size_t)(K / kUnitK) + ku) *
+                                                  (size_t)unit_bytes);
+  for (int q = threadIdx.x; q < unit_bytes / 16; q += blockDim.x) {
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (q < kQwStage / 16) {
+      const int blk = q >> 7, r = (q >> 3) & 15, c = (q & 7) ^ (r & 7);
+      const int col = tile * kTileN + blk * 32 + c * 4;
+      const size_t row = (size_t)ku * 16 + r;
+      if (col < N)  // N % 32 == 0: a chunk is wholly inside or wholly past N
+        for (int i = 0; i < 4; ++i) w[i] = qw[row * N + col + i];
+    } else if (q < kQwStage / 16 + sc_chunks) {
+      const int i16 = q - kQwStage / 16, g = i16 >> 4, col = tile * kTileN + (i16 & 15) * 8;
+      if (col < N) {
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(sc + (size_t)(grow0 + g) * N + col);
+        for (int i = 0; i < 4; ++i) w[i] = src[i];
+      }
+    } else {
+      const int i16 = q - kQwStage / 16 - sc_chunks, g = i16 >> 2;
+      const int wcol = tile * (kTileN / 8) + (i16 & 3) * 4;
+      if (wcol < N / 8)
+        for (int i = 0; i < 4; ++i) w[i] = qz[(size_t)(grow0 + g) * (N / 8) + wcol + i];
+    }
+    dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 }  // namespace
 
 int launch_w4(const void* a, const void* qw, const void* qz, const void* sc, void* y, int M, int K,
@@ -1610,6 +1708,41 @@ int launch_w4(const void* a, const void* qw, const void* qz, const void* sc, voi
   if (rc) return rc;
   return dispatch<false>(make_args(a, y, M, K, N, G, ws), qw, qz, sc, nullptr, stream,
                          /*early=*/true);
+}
+
+size_t w4_packed_bytes(int K, int N, int G) {
+  if (K < kUnitK || K % kUnitK != 0 || N < 32 || N % 32 != 0 ||
+      !(G == 32 || G == 64 || (G >= kUnitK && G % kUnitK == 0)) || K % G != 0)
+    return 0;
+  return (size_t)((N + kTileN - 1) / kTileN) * (size_t)(K / kUnitK) * (size_t)packed_unit_bytes(G);
+}
+
+int w4_repack(const void* qw, const void* qz, const void* sc, int K, int N, int G, void* out,
+              size_t out_bytes, cudaStream_t stream) {
+  int rc = validate(qw, qw, qz, sc, out, 1, K, N, G);
+  if (rc) return rc;
+  if (!aligned16(out)) return fail(B2_ERR_INVALID_ARG, "w4_repack: out must be 16-byte aligned");
+  const size_t need = w4_packed_bytes(K, N, G);
+  if (out_bytes < need)
+    return fail(B2_ERR_INVALID_ARG, "w4_repack: out holds %zu bytes, needs %zu", out_bytes, need);
+  const dim3 grid((unsigned)(K / kUnitK), (unsigned)((N + kTileN - 1) / kTileN));
+  w4_repack_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint32_t*>(qw),
+                                             static_cast<const uint32_t*>(qz),
+                                             static_cast<const __half*>(sc),
+                                             static_cast<uint8_t*>(out), K, N, G,
+                                             packed_unit_bytes(G));
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+
+int launch_w4_packed(const void* a, const void* packed, void* y, int M, int K, int N, int G,
+                     void* ws, size_t ws_bytes, cudaStream_t stream) {
+  int rc = validate(a, packed, packed, packed, y, M, K, N, G, ws, ws_bytes);
+  if (rc) return rc;
+  W4Args args = make_args(a, y, M, K, N, G, ws);
+  args.pk = static_cast<const uint8_t*>(packed);
+  args.pk_unit = packed_unit_bytes(G);
+  return dispatch<false>(args, nullptr, nullptr, nullptr, nullptr, stream, /*early=*/true);
 }
 
 int launch_w4_noalloc(const void* a, const void* qw, const void* qz, const void* sc, void* y, int M,
@@ -1804,6 +1937,22 @@ extern "C" int b2_w4_gemm(const void* a, const void* qw, const void* qz, const v
                           void* stream) {
   return b2::launch_w4(a, qw, qz, sc, y, M, K, N, group_size, ws, ws_bytes,
                        static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t b2_w4_packed_bytes(int K, int N, int group_size) {
+  return b2::w4_packed_bytes(K, N, group_size);
+}
+
+extern "C" int b2_w4_repack(const void* qw, const void* qz, const void* sc, int K, int N,
+                            int group_size, void* out, size_t out_bytes, void* stream) {
+  return b2::w4_repack(qw, qz, sc, K, N, group_size, out, out_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int b2_w4_gemm_packed(const void* a, const void* packed, void* y, int M, int K, int N,
+                                 int group_size, void* ws, size_t ws_bytes, void* stream) {
+  return b2::launch_w4_packed(a, packed, y, M, K, N, group_size, ws, ws_bytes,
+                              static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int b2_w4_gemm_allreduce(b2_nvar* ar, const void* a, const void* qw, const void* qz,

@@ -90,6 +90,45 @@ def w4_ref_columns(x, qw, qz, sc, cols: np.ndarray) -> np.ndarray:
     return sub[:, [pos[c] for c in cols]]
 
 
+def w4_repack(qw: np.ndarray, qz: np.ndarray, sc: np.ndarray, G: int) -> np.ndarray:
+    """Byte image of the load-time repack (B200 addition; the reference streams qw, qz and sc
+    from their GPTQ layouts, kernels/w4.cu:477-478): uint8[tiles, K/128, unit] where unit (tile,
+    ku) is the shared-memory image of its 128 columns x 128 k -
+      qw  [4 blocks of 32 columns][16 word rows][8 chunks of 4 words], chunk c of word row r stored
+          at slot c ^ (r & 7) (the 128-byte swizzle of the tensor copy);
+      sc  the unit's RG = max(1, 128 / G) group rows of 128 fp16;
+      qz  the same rows' 16 zero words;
+    columns past N are zero. A permutation of bytes only: the GEMM on it must equal the GEMM on
+    the original tensors bit for bit."""
+    qw = np.ascontiguousarray(qw).view(np.uint32)
+    qz = np.ascontiguousarray(qz).view(np.uint32)
+    sc = np.ascontiguousarray(sc).view(np.uint16)
+    K8, N = qw.shape
+    K = K8 * 8
+    tiles, kus = (N + 127) // 128, K // 128
+    RG = 1 if G >= 128 else 128 // G
+    Np = tiles * 128
+    qwp = np.zeros((K8, Np), np.uint32)
+    qwp[:, :N] = qw
+    scp = np.zeros((K // G, Np), np.uint16)
+    scp[:, :N] = sc
+    qzp = np.zeros((K // G, Np // 8), np.uint32)
+    qzp[:, : N // 8] = qz
+    # (ku, r, tile, block, chunk, word) -> (tile, ku, block, r, chunk, word)
+    q = qwp.reshape(kus, 16, tiles, 4, 8, 4).transpose(2, 0, 3, 1, 4, 5)
+    slot_src = np.array([[s ^ (r & 7) for s in range(8)] for r in range(16)])  # slot s <- chunk
+    q = np.take_along_axis(q, slot_src[None, None, None, :, :, None], axis=4)
+    rows = np.array([(ku * 128) // G + g for ku in range(kus) for g in range(RG)]).reshape(kus, RG)
+    s = scp[rows].reshape(kus, RG, tiles, 128).transpose(2, 0, 1, 3)      # (tile, ku, g, 128)
+    z = qzp[rows].reshape(kus, RG, tiles, 16).transpose(2, 0, 1, 3)       # (tile, ku, g, 16)
+    out = np.concatenate([
+        np.ascontiguousarray(q).view(np.uint8).reshape(tiles, kus, -1),
+        np.ascontiguousarray(s).view(np.uint8).reshape(tiles, kus, -1),
+        np.ascontiguousarray(z).view(np.uint8).reshape(tiles, kus, -1)], axis=2)
+    assert out.shape[2] == 8192 + RG * 320
+    return out
+
+
 def gemm_ref(x: np.ndarray, w: np.ndarray) -> np.ndarray:
     """float64 reference y[M, N] = x @ w^T for w[N, K] (kernels/bench_skinny.py:44, in float64)."""
     return x.astype(np.float64) @ w.astype(np.float64).T

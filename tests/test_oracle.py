@@ -158,3 +158,32 @@ def test_generators_are_seeded(oracle):
     x, qw, qz, sc = a
     assert x.dtype == np.float16 and qw.dtype == np.int32 and qz.dtype == np.int32
     assert sc.dtype == np.float16 and sc.min() >= 0.005 and sc.max() <= 0.02
+
+
+@pytest.mark.parametrize("K,N,G", [(256, 96, 32), (512, 352, 64), (1024, 384, 128), (1024, 160, 256)])
+def test_repack_image_inverts(oracle, K, N, G):
+    """The repack image holds every qw word, scale and zero of its unit at the documented place
+    (block w, word row r, chunk c at w * 2048 + r * 128 + ((c ^ (r & 7)) << 4); then the group
+    rows of scales and zeros), and zeros past N."""
+    _, qw, qz, sc = oracle.gen_w4(2, K, N, G, seed=K + N)
+    img = oracle.w4_repack(qw, qz, sc, G)
+    RG = 1 if G >= 128 else 128 // G
+    tiles, kus, unit = img.shape
+    assert (tiles, kus, unit) == ((N + 127) // 128, K // 128, 8192 + RG * 320)
+    qwu, scu, qzu = qw.view(np.uint32), sc.view(np.uint16), qz.view(np.uint32)
+    for t in range(tiles):
+        cols = np.arange(t * 128, t * 128 + 128)
+        inside = cols < N
+        for ku in range(kus):
+            words = img[t, ku, :8192].view(np.uint32).reshape(4, 16, 8, 4)
+            for r in range(16):
+                logical = words[:, r, [c ^ (r & 7) for c in range(8)], :].reshape(128)
+                exp = np.where(inside, qwu[ku * 16 + r, np.minimum(cols, N - 1)], 0)
+                assert (logical == exp).all(), (t, ku, r)
+            s = img[t, ku, 8192:8192 + RG * 256].view(np.uint16).reshape(RG, 128)
+            z = img[t, ku, 8192 + RG * 256:].view(np.uint32).reshape(RG, 16)
+            for g in range(RG):
+                row = (ku * 128) // G + g
+                assert (s[g] == np.where(inside, scu[row, np.minimum(cols, N - 1)], 0)).all()
+                wc = np.arange(t * 16, t * 16 + 16)
+                assert (z[g] == np.where(wc < N // 8, qzu[row, np.minimum(wc, N // 8 - 1)], 0)).all()

@@ -1,0 +1,141 @@
+"""W4A16 on weights repacked at load time (b2_w4_repack / b2_w4_gemm_packed), through the C ABI.
+
+The repack is a byte permutation, so its output is compared byte for byte with the oracle's
+restatement, and the packed GEMM must equal the GEMM on the original tensors bit for bit (same
+plan, same bytes in shared memory); both are also checked against the float64 reference
+(kernels/check_w4.py:11-21)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import (check, dev, mismatch, sample_columns, stream_ptr, w4_device_inputs,
+                      w4_ref_sampled, workspace)
+
+pytestmark = pytest.mark.gpu
+
+
+def repack(capi, qw, qz, sc, K, N, G) -> torch.Tensor:
+    lib = capi.lib()
+    nbytes = lib.b2_w4_packed_bytes(K, N, G)
+    assert nbytes > 0
+    out = torch.full((nbytes,), 0xAB, dtype=torch.uint8, device="cuda")  # every byte is written
+    capi.check(lib.b2_w4_repack(qw.data_ptr(), qz.data_ptr(), sc.data_ptr(), K, N, G,
+                                out.data_ptr(), nbytes, stream_ptr()), "b2_w4_repack")
+    return out
+
+
+def gemm(capi, ws, x, qw, qz, sc, K, N, G) -> torch.Tensor:
+    y = torch.full((x.shape[0], N), float("nan"), dtype=torch.float16, device="cuda")
+    capi.check(capi.lib().b2_w4_gemm(x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(),
+                                     y.data_ptr(), x.shape[0], K, N, G, ws.data_ptr(), ws.numel(),
+                                     stream_ptr()), "b2_w4_gemm")
+    return y
+
+
+def gemm_packed(capi, ws, x, pk, K, N, G) -> torch.Tensor:
+    y = torch.full((x.shape[0], N), float("nan"), dtype=torch.float16, device="cuda")
+    capi.check(capi.lib().b2_w4_gemm_packed(x.data_ptr(), pk.data_ptr(), y.data_ptr(), x.shape[0],
+                                            K, N, G, ws.data_ptr(), ws.numel(), stream_ptr()),
+               "b2_w4_gemm_packed")
+    return y
+
+
+SMALL = [(1, 128, 32, 128), (3, 256, 96, 32), (5, 512, 352, 64), (8, 1024, 384, 128),
+         (7, 1024, 160, 256), (8, 2176, 5120, 128), (2, 4096, 1056, 32)]
+
+
+@pytest.mark.parametrize("M,K,N,G", SMALL)
+def test_repack_bytes_match_oracle(capi, oracle, M, K, N, G):
+    _, qw, qz, sc = oracle.gen_w4(M, K, N, G, seed=K + N + G)
+    pk = repack(capi, dev(qw), dev(qz), dev(sc), K, N, G)
+    torch.cuda.synchronize()
+    ref = oracle.w4_repack(qw, qz, sc, G).reshape(-1)
+    got = pk.cpu().numpy()
+    assert got.shape == ref.shape
+    bad = np.flatnonzero(got != ref)
+    assert bad.size == 0, f"{bad.size} bytes differ, first at {bad[:8]}"
+
+
+@pytest.mark.parametrize("path", [0, 1, 2], ids=["auto", "stream-K", "cluster"])
+@pytest.mark.parametrize("M,K,N,G", SMALL)
+def test_packed_equals_unpacked(capi, oracle, path, M, K, N, G):
+    """Each split-K kernel on packed weights gives the bits of the same kernel on the original
+    tensors (forced with B2_TUNE_W4_PATH), and both are within tolerance of the oracle."""
+    lib = capi.lib()
+    saved = lib.b2_get_tuning(4)
+    lib.b2_set_tuning(4, path)
+    try:
+        ws = workspace(capi)
+        x, qw, qz, sc = oracle.gen_w4(M, K, N, G, seed=M + K + N + G)
+        xd, qwd, qzd, scd = dev(x), dev(qw), dev(qz), dev(sc)
+        pk = repack(capi, qwd, qzd, scd, K, N, G)
+        y0 = gemm(capi, ws, xd, qwd, qzd, scd, K, N, G)
+        y1 = gemm_packed(capi, ws, xd, pk, K, N, G)
+        assert torch.equal(y0, y1), mismatch(y0, y1)
+        check(y1, oracle.w4_ref(x, qw, qz, sc), f"packed path {path} M={M} K={K} N={N} G={G}")
+        torch.cuda.synchronize()
+        assert int(ws[:4].view(torch.int32).item()) == 0
+    finally:
+        lib.b2_set_tuning(4, saved)
+
+
+@pytest.mark.parametrize("name,M,K,N", [("cfg0", 7, 4096, 4096), ("gate_up", 8, 5120, 34816),
+                                        ("down", 8, 17408, 5120), ("qkv", 8, 5120, 8192)])
+def test_packed_full_size(capi, name, M, K, N):
+    """BASELINE shapes: bit-equal to the unpacked GEMM over the whole output (a size-independent
+    property), sampled columns against the float64 reference, and the original tensors may be
+    freed once the repack has completed."""
+    G = 128
+    ws = workspace(capi)
+    x, qw, qz, sc = w4_device_inputs(M, K, N, G, seed=N)
+    y0 = gemm(capi, ws, x, qw, qz, sc, K, N, G)
+    pk = repack(capi, qw, qz, sc, K, N, G)
+    torch.cuda.synchronize()
+    cols = sample_columns(N, 300, seed=1)
+    ref = w4_ref_sampled(x, qw, qz, sc, cols)
+    del qw, qz, sc
+    torch.cuda.empty_cache()
+    y1 = gemm_packed(capi, ws, x, pk, K, N, G)
+    assert torch.equal(y0, y1), f"{name}: {mismatch(y0, y1)}"
+    check(y1[:, torch.from_numpy(cols).cuda()], ref, name)
+
+
+def test_packed_graph_replay(capi, oracle):
+    ws = workspace(capi)
+    K, N, G = 2048, 1024, 128
+    x, qw, qz, sc = oracle.gen_w4(4, K, N, G, seed=3)
+    xd = dev(x)
+    pk = repack(capi, dev(qw), dev(qz), dev(sc), K, N, G)
+    y = torch.empty(4, N, dtype=torch.float16, device="cuda")
+    lib = capi.lib()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            capi.check(lib.b2_w4_gemm_packed(xd.data_ptr(), pk.data_ptr(), y.data_ptr(), 4, K, N,
+                                             G, ws.data_ptr(), ws.numel(), s.cuda_stream), "packed")
+    torch.cuda.current_stream().wait_stream(s)
+    x2, _, _, _ = oracle.gen_w4(4, K, N, G, seed=4)
+    xd.copy_(dev(x2))
+    g.replay()
+    torch.cuda.synchronize()
+    check(y, oracle.w4_ref(x2, qw, qz, sc), "graph replay")
+
+
+def test_packed_rejects(capi):
+    lib = capi.lib()
+    assert lib.b2_w4_packed_bytes(100, 64, 128) == 0      # K % 128
+    assert lib.b2_w4_packed_bytes(128, 48, 128) == 0      # N % 32
+    assert lib.b2_w4_packed_bytes(384, 64, 96) == 0       # group size outside the contract
+    K, N, G = 256, 64, 128
+    t = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    p = t.data_ptr()
+    need = lib.b2_w4_packed_bytes(K, N, G)
+    assert lib.b2_w4_repack(p, p, p, K, N, G, p, need - 16, stream_ptr()) != 0   # too small
+    assert lib.b2_w4_repack(p, p, p, K, N, G, p + 8, need, stream_ptr()) != 0    # misaligned
+    assert lib.b2_w4_gemm_packed(p, 0, p, 1, K, N, G, p, t.numel(), stream_ptr()) != 0  # null
