@@ -295,6 +295,11 @@ int b2_w4_gemm_allreduce_emulated(b2_nvar* const* handles, int ranks, const void
 #define B2_TUNE_AR_TWO_SHOT 7     /* fused all-reduce in the cluster kernel: 0 = two-shot from 4
                                      ranks up (each tile reduced at one owner rank, the result
                                      sent back), 1 = always two-shot, 2 = always one-shot        */
+#define B2_TUNE_W4_NO_ALIAS 8     /* cluster path, G >= 128, no exchange: when every cluster has
+                                     one output tile and every CTA at least 16 k-units, its
+                                     reduction buffers take the place of the drained stage ring,
+                                     which leaves room for a fifth stage; nonzero keeps them
+                                     apart (four stages)                                         */
 int b2_set_tuning(int key, int value);
 int b2_get_tuning(int key);
 

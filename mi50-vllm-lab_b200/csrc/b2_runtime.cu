@@ -202,7 +202,8 @@ size_t ws_total_bytes() { return ws_norm_offset() + (size_t)kWsMaxCtas * kMaxM *
 // ----------------------------------------------------------------------------------------------
 // Tuning
 // ----------------------------------------------------------------------------------------------
-static std::atomic<int> g_tune[8];
+constexpr int kTuneKeys = 16;
+static std::atomic<int> g_tune[kTuneKeys];
 
 // B2_TUNE="key=value,key=value" in the environment presets tuning keys (read once, before the
 // first use; b2_set_tuning overrides).
@@ -219,7 +220,7 @@ static void tuning_from_env() {
       p = end + 1;
       const long v = std::strtol(p, &end, 10);
       if (end == p) break;
-      if (k >= 0 && k < 8) g_tune[k].store((int)v);
+      if (k >= 0 && k < kTuneKeys) g_tune[k].store((int)v);
       p = end;
       if (*p == ',') ++p;
     }
@@ -228,7 +229,7 @@ static void tuning_from_env() {
 
 int tuning(int key) {
   tuning_from_env();
-  return (key >= 0 && key < 8) ? g_tune[key].load() : 0;
+  return (key >= 0 && key < kTuneKeys) ? g_tune[key].load() : 0;
 }
 
 int streamk_ctas(long long total, int sm_count, int occ, int min_units_default) {
@@ -291,7 +292,7 @@ int b2_workspace_status(void* ws, int clear, int* device_status) {
 
 int b2_set_tuning(int key, int value) {
   tuning_from_env();
-  if (key < 0 || key >= 8) return fail(B2_ERR_INVALID_ARG, "unknown tuning key %d", key);
+  if (key < 0 || key >= kTuneKeys) return fail(B2_ERR_INVALID_ARG, "unknown tuning key %d", key);
   g_tune[key].store(value);
   return B2_OK;
 }

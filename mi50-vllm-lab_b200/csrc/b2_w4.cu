@@ -830,9 +830,13 @@ __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
 // and CTA r adds column slice r of all CS partials in rank order (deterministic) and writes it.
 // No workspace, no global atomics, no second pass; the fused all-reduce pushes each slice.
 // =================================================================================================
-template <int GP>
+// A (aliased): every cluster of the launch reduces exactly one output tile, so its reduction
+// buffers are needed only once the stage ring has drained; they then take the place of the first
+// stages' weights, and the 8.6 KB they would hold apart buys a fifth stage instead.
+template <int GP, bool A = false>
 struct CfgC {
-  static constexpr int kStages = 4;  // 4 stages + a 4 KB reduction buffer: four CTAs per SM
+  // 4 stages + a 4 KB reduction buffer, or 5 stages with the buffers aliased: four CTAs per SM
+  static constexpr int kStages = A ? 5 : 4;
   static constexpr int RG = 4 / GP;
   static constexpr int kScBytes = RG * kTileN * 2;
   static constexpr int kQzBytes = RG * (kTileN / 8) * 4;
@@ -845,22 +849,25 @@ struct CfgC {
   static constexpr int kQzOff = kScOff + kStages * kScStride;
   // reduction buffers: my partial tile arranged by destination CTA ([8 rows][W_r] fp32 per CTA
   // r), and the CS slices the cluster sends me ([CS][8 rows][W] fp32, W <= 128 / CS + 1)
-  static constexpr int kSendOff = kQzOff + kStages * kQzStride;
+  static constexpr int kRingEnd = kQzOff + kStages * kQzStride;
+  static constexpr int kSendOff = A ? 0 : kRingEnd;
   static constexpr int kRecvOff = kSendOff + kMaxM * kTileN * 4;
   static constexpr int kRecvBytes = kMaxM * (kTileN + 16) * 4;
-  static constexpr int kBarOff = kRecvOff + kRecvBytes;
+  static constexpr int kBarOff = A ? kRingEnd : kRecvOff + kRecvBytes;
   static constexpr int kNormOff = align128(kBarOff + (2 * kStages + 3) * 8 + 32);
   static constexpr int kSmem = 1024 + kNormOff + kNormFloats * 4;
   static_assert(kXOff % 1024 == 0 && kXBytes % 1024 == 0, "swizzled boxes need 1024 B");
   static_assert(kScOff % 128 == 0 && kQzOff % 128 == 0 && kSendOff % 128 == 0 &&
                     kRecvOff % 128 == 0, "alignment");
+  static_assert(!A || kRecvOff + kRecvBytes <= kXOff, "aliased buffers lie inside the qw ring");
 };
 
-template <int GP, bool FUSED>
+template <int GP, bool FUSED, bool A = false>
 __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtensorMap& tm_sc,
                                         const CUtensorMap& tm_qz, const CUtensorMap& tm_x,
                                         const W4Args& p, const ArView& ar) {
-  using C = CfgC<GP>;
+  static_assert(!(A && FUSED), "the exchange epilogue keeps its buffers apart");
+  using C = CfgC<GP, A>;
   constexpr int kStages = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -888,6 +895,10 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
   const int k0 = upt * crank / CS, k1 = upt * (crank + 1) / CS, nk = k1 - k0;
   const int ntile = (tiles - 1 - cid) / NC + 1;
   const int n_units = ntile * nk;
+  if (A && ntile != 1) {  // the host launches the aliased layout only with one tile per cluster
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, B2_ERR_STATE);
+    return;  // the whole cluster returns (ntile is the same for all its CTAs)
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -1023,10 +1034,17 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
     // slices it received in cluster rank order from its own shared memory. With one tile per
     // CTA there is no round trip at all; with more, the next tile's copies wait until every
     // receiver has added up the previous one (red_empty).
-    // (a) the send buffer: the copies that read it for the previous tile must be done reading
+    // (a) the send buffer: the copies that read it for the previous tile must be done reading.
+    // Aliased layout: the buffers lie on the stage ring, so every consumer warp must be done with
+    // the ring before they are written, and no peer may push into my receive buffer before I say
+    // so: lane r arrives on CTA r's red_empty, and CTA r pushes only once all CS CTAs have.
     if (it > 0) {
       if (tid < CS) bulk_wait_read_all();
       named_bar_sync(1, kWarps * 32);
+    }
+    if (A) {
+      named_bar_sync(1, kWarps * 32);
+      if (tid < CS) mbar_arrive_remote(mapa_shared(smem_u32(red_empty), (uint32_t)tid));
     }
     {
       const float v[2][4] = {{acc[0][0], acc[0][2], acc[1][0], acc[1][2]},   // row 2t
@@ -1049,7 +1067,8 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
     named_bar_sync(1, kWarps * 32);
     // (b) lane r of warp 0 sends slice r into CTA r's receive buffer, at my rank's place
     if (tid < CS) {
-      const bool go = it == 0 || mbar_wait_cluster(red_empty, (uint32_t)((it - 1) & 1), s_abort);
+      const bool go = (it == 0 && !A) ||
+                      mbar_wait_cluster(red_empty, (uint32_t)((A ? it : it - 1) & 1), s_abort);
       if (go) {
         const int cr0 = kTileN * tid / CS, wr = kTileN * (tid + 1) / CS - cr0;
         const uint32_t bytes = (uint32_t)(kMaxM * wr * 4);
@@ -1219,7 +1238,8 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
       *no_abort = 0;
       mbar_wait_cluster(red_full, (uint32_t)((ntile - 1) & 1), no_abort);
       *no_abort = 0;
-      if (ntile > 1) mbar_wait_cluster(red_empty, (uint32_t)((ntile - 2) & 1), no_abort);
+      if (A) mbar_wait_cluster(red_empty, 0u, no_abort);  // every peer's "drained" arrival
+      else if (ntile > 1) mbar_wait_cluster(red_empty, (uint32_t)((ntile - 2) & 1), no_abort);
       *no_abort = 0;
       if (FUSED && !p.ll && crank == 0)
         mbar_wait_cluster(pub_bar, (uint32_t)((ntile - 1) & 1), no_abort);
@@ -1230,12 +1250,12 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
   if (!ok && lane == 0) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
 }
 
-template <int GP, bool FUSED>
+template <int GP, bool FUSED, bool A = false>
 __global__ void __launch_bounds__(kThreads, GP == 4 ? 4 : 3)
     w4c_kernel(const __grid_constant__ CUtensorMap tm_qw, const __grid_constant__ CUtensorMap tm_sc,
                const __grid_constant__ CUtensorMap tm_qz, const __grid_constant__ CUtensorMap tm_x,
                const __grid_constant__ W4Args p, const __grid_constant__ ArView ar) {
-  w4c_body<GP, FUSED>(tm_qw, tm_sc, tm_qz, tm_x, p, ar);
+  w4c_body<GP, FUSED, A>(tm_qw, tm_sc, tm_qz, tm_x, p, ar);
 }
 
 // =================================================================================================
@@ -1318,14 +1338,14 @@ struct ClusterCaps {
   bool configured = false;
   int max_clusters[17] = {0};
 };
-ClusterCaps g_ccaps[64][3][2];
+ClusterCaps g_ccaps[64][3][2][2];
 
-template <int GP, bool FUSED>
+template <int GP, bool FUSED, bool A = false>
 int cluster_caps(int dev, const ClusterCaps** out) {
-  using C = CfgC<GP>;
-  ClusterCaps& cc = g_ccaps[dev][GP == 1 ? 0 : GP == 2 ? 1 : 2][FUSED ? 1 : 0];
+  using C = CfgC<GP, A>;
+  ClusterCaps& cc = g_ccaps[dev][GP == 1 ? 0 : GP == 2 ? 1 : 2][FUSED ? 1 : 0][A ? 1 : 0];
   if (!cc.configured) {
-    auto kern = w4c_kernel<GP, FUSED>;
+    auto kern = w4c_kernel<GP, FUSED, A>;
     B2_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem));
     // clusters of more than 8 CTAs are allowed on this part when asked for
     const bool big = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
@@ -1383,6 +1403,7 @@ double plan_clusters(const ClusterCaps& cc, int tiles, int upt, int want, int ma
 struct Plan {
   StreamK sk;
   int cs = 0, nc = 0;
+  bool alias = false;  // cluster kernel with its reduction buffers on the drained ring
 };
 
 // `share`: the launch gets 1/share of the GPU (several emulated ranks in one launch).
@@ -1452,6 +1473,18 @@ int make_plan(const W4Args& a, int max_ctas, Plan* out, int share = 1) {
     if (cost > 0.0 && (path == 2 || cost <= sk_cost) && (!a.norm || nc * cs <= kWsMaxCtas)) {
       pl.cs = cs;
       pl.nc = nc;
+      // One tile per cluster and a long k-range per CTA: the variant with a fifth stage. Its
+      // "drained" handshake costs a cluster round trip before the first push, which a long
+      // k-range repays: gate_up (20 units per CTA, clusters of 2) 25.7 -> 24.5 us, while with
+      // 3 to 11 units per CTA and clusters of 6 to 14 every shape lost 0.3 to 1 us.
+      if constexpr (GP == 4 && !FUSED) {
+        if (nc >= sk.tiles && (sk.upt + cs - 1) / cs >= 16 && !tuning(B2_TUNE_W4_NO_ALIAS)) {
+          const ClusterCaps* ca = nullptr;
+          rc = cluster_caps<GP, FUSED, true>(dev, &ca);
+          if (rc) return rc;
+          pl.alias = ca->max_clusters[cs] / occ_share >= nc;
+        }
+      }
     }
   }
   *out = pl;
@@ -1471,6 +1504,12 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
   if (pl.cs > 0) {
     a.cl_size = pl.cs;
     a.cl_count = pl.nc;
+    if constexpr (GP == 4 && !FUSED) {
+      if (pl.alias)
+        return launch_kernel_clusters(w4c_kernel<GP, FUSED, true>, pl.nc * pl.cs, pl.cs, kThreads,
+                                      CfgC<GP, true>::kSmem, stream, early, m_qw, m_sc, m_qz, m_x,
+                                      a, view);
+    }
     return launch_kernel_clusters(w4c_kernel<GP, FUSED>, pl.nc * pl.cs, pl.cs, kThreads,
                                   CfgC<GP>::kSmem, stream, early, m_qw, m_sc, m_qz, m_x, a, view);
   }

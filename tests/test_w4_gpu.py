@@ -210,3 +210,32 @@ def test_rejects_bad_inputs(ops):
         ops.w4gemm(a, qw, qz[:3], sc[:3], 128, 14)  # K % G
     with pytest.raises(RuntimeError):
         ops.w4gemm(torch.zeros(9, 512, dtype=torch.float16, device="cuda"), qw, qz, sc, 128, 14)
+
+
+@pytest.mark.parametrize("M,K,N", [(8, 5120, 34816), (8, 17408, 5120), (7, 4096, 4096), (3, 2176, 5120),
+                                   (1, 5120, 1024)])
+def test_cluster_aliased_buffers_same_bits(capi, ops, M, K, N):
+    """With one tile per cluster and long k-ranges the cluster kernel keeps its reduction buffers
+    on the drained stage ring and runs five stages; B2_TUNE_W4_NO_ALIAS keeps them apart (four
+    stages); forced to one cluster size so that both layouts run on every shape here. Same
+    sums in the same order, so the outputs must be identical, and sampled columns match the
+    float64 reference."""
+    lib = capi.lib()
+    saved = lib.b2_get_tuning(8)
+    x, qw, qz, sc = w4_device_inputs(M, K, N, 128, seed=K + N)
+    saved_cs = lib.b2_get_tuning(5)
+    try:
+        lib.b2_set_tuning(5, 1)  # clusters of one CTA: every CTA has the whole k-range
+        lib.b2_set_tuning(8, 0)
+        y_alias = run(ops, x, qw, qz, sc)
+        y_alias2 = run(ops, x, qw, qz, sc)
+        lib.b2_set_tuning(8, 1)
+        y_apart = run(ops, x, qw, qz, sc)
+    finally:
+        lib.b2_set_tuning(8, saved)
+        lib.b2_set_tuning(5, saved_cs)
+    assert torch.equal(y_alias, y_alias2), mismatch(y_alias, y_alias2)
+    assert torch.equal(y_alias, y_apart), mismatch(y_alias, y_apart)
+    cols = sample_columns(N, 200, seed=2)
+    check(y_alias[:, torch.from_numpy(cols).cuda()], w4_ref_sampled(x, qw, qz, sc, cols), f"{M}x{K}x{N}")
+    assert ops.workspace_status(False) == 0
