@@ -703,18 +703,29 @@ def run_profile(args):
     lib = capi.lib()
     torch.cuda.set_device(0)
     ws = torch.zeros(lib.b2_workspace_bytes(0), dtype=torch.uint8, device="cuda")
-    name, kind, M, K, N, G = next(w for w in PROFILE_ONLY + list(SWEEP) if args.only in w[0])
+    for kv in args.tune:
+        k, v = (int(t) for t in kv.split("="))
+        capi.check(lib.b2_set_tuning(k, v), "b2_set_tuning")
+    cases = PROFILE_ONLY + list(SWEEP)  # an exact workload name, else the first that contains it
+    name, kind, M, K, N, G = next((w for w in cases if args.only == w[0]), None) or \
+        next(w for w in cases if args.only in w[0])
     g = torch.Generator(device="cuda").manual_seed(5)
     x = torch.randn(M, K, device="cuda", generator=g).half()
     y = torch.empty(M, N, dtype=torch.float16, device="cuda")
     sp = torch.cuda.current_stream().cuda_stream
-    if kind == "w4":
+    if kind in ("w4", "w4p"):
         qw = torch.randint(-2**31, 2**31 - 1, (K // 8, N), device="cuda", dtype=torch.int32, generator=g)
         qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda", dtype=torch.int32, generator=g)
         sc = (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half()
         step = lambda: capi.check(lib.b2_w4_gemm(x.data_ptr(), qw.data_ptr(), qz.data_ptr(),  # noqa: E731
                                                  sc.data_ptr(), y.data_ptr(), M, K, N, G,
                                                  ws.data_ptr(), ws.numel(), sp))
+        if kind == "w4p":
+            pk = torch.empty(lib.b2_w4_packed_bytes(K, N, G), dtype=torch.uint8, device="cuda")
+            capi.check(lib.b2_w4_repack(qw.data_ptr(), qz.data_ptr(), sc.data_ptr(), K, N, G,
+                                        pk.data_ptr(), pk.numel(), sp), "b2_w4_repack")
+            step = lambda: capi.check(lib.b2_w4_gemm_packed(  # noqa: E731
+                x.data_ptr(), pk.data_ptr(), y.data_ptr(), M, K, N, G, ws.data_ptr(), ws.numel(), sp))
     else:
         w = (torch.randn(N, K, device="cuda", generator=g) * 0.02).half()
         step = lambda: capi.check(lib.b2_gemm_f16(x.data_ptr(), w.data_ptr(), y.data_ptr(), M, K,  # noqa: E731
