@@ -859,6 +859,10 @@ def main():
     ap.add_argument("--only", default="", help="with --sweep: workloads whose name contains one of these comma-separated "
                          "strings; with --profile: the first workload whose name contains it")
     ap.add_argument("--profile", action="store_true", help="eager launches of one --only workload (for ncu)")
+    ap.add_argument("--trace", default="", metavar="M,K,N[,G]",
+                    help="per-unit timeline of one W4 cluster-kernel launch (trace build: "
+                         "python mi50-vllm-lab_b200/builder.py --trace)")
+    ap.add_argument("--trace-units", action="store_true", help="with --trace: the raw stamps too")
     ap.add_argument("--norm-epilogue", action="store_true",
                     help="row-parallel W4 layer + residual add + RMSNorm: fused vs separate, 1 GPU")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
@@ -872,6 +876,16 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.trace:
+        import __graft_entry__ as entry
+
+        entry.load_package()
+        from mi50_vllm_lab_b200 import trace_w4
+
+        argv = args.trace.split(",") + (["--units"] if args.trace_units else [])
+        for kv in args.tune:
+            argv += ["--tune", kv]
+        print(json.dumps(trace_w4.main(argv)))
     elif args.profile:
         run_profile(args)
     elif args.sweep:

@@ -101,6 +101,30 @@ def build_torch_ops(verbose: bool = False) -> Path:
     return TORCH_LIB
 
 
+TRACE_LIB = HERE / "libb2skinny_trace.so"
+
+
+def build_trace(verbose: bool = False) -> Path:
+    """The C ABI again with -DB2_TRACE: the cluster kernel stamps a per-unit timeline (see
+    trace_w4.py). Built only on request; the product library compiles none of the stamps."""
+    tdir = BUILD / "trace"
+    tdir.mkdir(parents=True, exist_ok=True)
+    deps = [CSRC / h for h in HEADERS] + [INCLUDE / "b2_skinny.h"]
+    objs = []
+    for src in CU_SOURCES:
+        obj = tdir / (src + ".o")
+        objs.append(obj)
+        if _newer(obj, [CSRC / src] + deps):
+            _run([NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+                  "--expt-relaxed-constexpr", "-DB2_TRACE", f"-I{INCLUDE}", f"-I{CSRC}", "-c",
+                  str(CSRC / src), "-o", str(obj)], verbose)
+    if _newer(TRACE_LIB, objs):
+        tmp = tdir / TRACE_LIB.name
+        _run([NVCC, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lrt"], verbose)
+        shutil.move(str(tmp), TRACE_LIB)
+    return TRACE_LIB
+
+
 def build(verbose: bool = False) -> tuple[Path, Path]:
     BUILD.mkdir(exist_ok=True)
     capi = build_capi(verbose)
@@ -112,5 +136,7 @@ if __name__ == "__main__":
     v = "-v" in sys.argv
     if "--ptxas" in sys.argv:
         build_capi(verbose=True, ptxas_verbose=True)
+    elif "--trace" in sys.argv:
+        print(build_trace(verbose=v))
     else:
         print(build(verbose=v))

@@ -862,6 +862,24 @@ struct CfgC {
   static_assert(!A || kRecvOff + kRecvBytes <= kXOff, "aliased buffers lie inside the qw ring");
 };
 
+// Timeline trace (builds with -DB2_TRACE only; the library proper compiles none of it): CTA 0 of
+// a cluster-kernel launch stamps the global timer per unit at the producer's issue (event 0), its
+// wait for a free stage (1), consumer warp 0's wait for the data (2) and its end of the unit (3),
+// and per tile at the start of the reduction (4); every CTA records its start, end and SM.
+#ifdef B2_TRACE
+constexpr int kTraceUnits = 4096, kTraceCtas = 4096;
+__device__ unsigned long long g_trace_units[5][kTraceUnits];
+__device__ unsigned long long g_trace_ctas[kTraceCtas][3];
+#define B2_TR(e, j)                                                                   \
+  do {                                                                                \
+    if (blockIdx.x == 0 && (j) < kTraceUnits) g_trace_units[e][j] = globaltimer_ns(); \
+  } while (0)
+#else
+#define B2_TR(e, j) \
+  do {              \
+  } while (0)
+#endif
+
 template <int GP, bool FUSED, bool A = false>
 __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtensorMap& tm_sc,
                                         const CUtensorMap& tm_qz, const CUtensorMap& tm_x,
@@ -915,6 +933,14 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
   __syncthreads();
   cluster_sync_all();  // no CTA arrives on a peer's barrier before the peer initialised it
   grid_dep_launch();
+#ifdef B2_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) {
+    unsigned int smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    g_trace_ctas[blockIdx.x][0] = globaltimer_ns();
+    g_trace_ctas[blockIdx.x][2] = smid;
+  }
+#endif
 
   // ------------------------------------------------------------------ producer warp (1 thread)
   if (warp == kWarps) {
@@ -939,6 +965,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
         const int n0 = tile * kTileN;
         if (with_w) {
           const int grow = (ku * kUnitK) / p.G;
+          B2_TR(0, j);
           mbar_arrive_expect_tx(&full[st], C::kTx);
           if (p.pk) {
             const uint8_t* u = packed_unit(p, tile, ku);
@@ -976,6 +1003,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
       uint32_t ph = 0;
       for (; issued < n_units; ++issued) {
         if (!mbar_wait_backoff(&empty[st], ph, s_abort)) break;
+        B2_TR(1, issued);
         issue(st, issued, true, true);
         if (++st == kStages) st = 0, ph ^= 1u;
       }
@@ -1017,6 +1045,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
     const int tile = cid + it * NC;
     for (int ku = k0; ku < k1; ++ku) {
       if (ok) ok = mbar_wait(&full[st], ph, s_abort);
+      if (warp == 0 && lane == 0) B2_TR(2, it * nk + ku - k0);
       __syncwarp();
       consume_unit<GP>(L, x_base0 + st * C::kXBytes, qw_base0 + st * kQwStage,
                        reinterpret_cast<const __half*>(s_sc + st * C::kScStride),
@@ -1024,8 +1053,10 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
       fence_proxy_async_smem();  // this lane's reads of the stage precede its next TMA fill
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
+      if (warp == 0 && lane == 0) B2_TR(3, it * nk + ku - k0);
       if (++st == kStages) st = 0, ph ^= 1u;
     }
+    if (warp == 0 && lane == 0) B2_TR(4, it);
 
     // ---------------------------------------------------------------- tile epilogue: reduce
     // Push, not pull: every CTA writes its partial tile into its send buffer arranged by the CTA
@@ -1248,6 +1279,9 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
     named_bar_sync(1, kWarps * 32);
   }
   if (!ok && lane == 0) atomicCAS(p.status, 0, B2_ERR_TIMEOUT);
+#ifdef B2_TRACE
+  if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) g_trace_ctas[blockIdx.x][1] = globaltimer_ns();
+#endif
 }
 
 template <int GP, bool FUSED, bool A = false>
@@ -2059,3 +2093,23 @@ extern "C" int b2_w4_plan(int M, int K, int N, int group_size, int fused, int* p
   *ctas = pl.cs > 0 ? pl.cs * pl.nc : pl.sk.ctas;
   return B2_OK;
 }
+
+#ifdef B2_TRACE
+// Copy the trace of the last traced launch to the host: units[5][4096] and ctas[4096][3] (64-bit
+// nanoseconds; SM ids in ctas[i][2]); entries not written are 0 or hold an earlier launch's.
+extern "C" int b2_trace_read(unsigned long long* units, unsigned long long* ctas) {
+  if (cudaMemcpyFromSymbol(units, b2::g_trace_units, sizeof(b2::g_trace_units)) != cudaSuccess ||
+      cudaMemcpyFromSymbol(ctas, b2::g_trace_ctas, sizeof(b2::g_trace_ctas)) != cudaSuccess)
+    return B2_ERR_CUDA;
+  return B2_OK;
+}
+extern "C" int b2_trace_clear() {
+  static unsigned long long zero[5 * 4096];
+  if (cudaMemcpyToSymbol(b2::g_trace_units, zero, sizeof(b2::g_trace_units)) != cudaSuccess ||
+      cudaMemcpyToSymbol(b2::g_trace_ctas, zero, sizeof(zero) < sizeof(b2::g_trace_ctas)
+                                                     ? sizeof(zero) : sizeof(b2::g_trace_ctas)) !=
+          cudaSuccess)
+    return B2_ERR_CUDA;
+  return B2_OK;
+}
+#endif
