@@ -28,6 +28,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -1371,6 +1372,7 @@ bool plan_log() {
 struct ClusterCaps {
   bool configured = false;
   int max_clusters[17] = {0};
+  int occ = 0;  // resident CTAs per SM
 };
 ClusterCaps g_ccaps[64][3][2][2];
 
@@ -1403,6 +1405,10 @@ int cluster_caps(int dev, const ClusterCaps** out) {
       if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess) cc.max_clusters[cs] = n;
       (void)cudaGetLastError();
     }
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&cc.occ, kern, kThreads, C::kSmem) !=
+        cudaSuccess)
+      cc.occ = 0;
+    (void)cudaGetLastError();
     cc.configured = true;
   }
   *out = &cc;
@@ -1410,12 +1416,19 @@ int cluster_caps(int dev, const ClusterCaps** out) {
 }
 
 // Cluster plan for `tiles` output tiles of `upt` k-units: the cluster size with the smallest
-// critical path (tiles per cluster x k-units per CTA, plus half a unit for the shared-memory
-// reduction when the tile is split). Returns the cost in unit-times, or a negative value when no
-// cluster size fits.
+// critical path. Returns the plain model's cost of the chosen size in unit-times (the scale of
+// the stream-K comparison), or a negative value when no cluster size fits.
+// Plain model (fused launches): tiles per cluster x (k-units per CTA + half a unit for the
+// reduction when the tile is split). Placement model (`occ` > 0, CTAs of the kernel per SM, on
+// `sms` SMs): clusters of cs CTAs fill at most max_clusters[cs] * cs / occ SMs (clusters of 11 to
+// 14 leave ~20 of 148 SMs without work), a CTA on an SM holding more than three runs 10 % slower
+// per extra CTA, and the reduction grows with the cluster (0.3 unit-times per CTA). Fitted on
+// forced cluster sizes 1..16 of seven shapes (config 0, config 2 at M = 8, config 4 TP=8
+// qkv/gate_up), where it picks the fastest size on every one: o_proj 9.4 -> 8.7 us and TP=8
+// qkv 5.3 -> 4.4 us against the plain model.
 double plan_clusters(const ClusterCaps& cc, int tiles, int upt, int want, int max_cs, int* cs_out,
-                     int* nc_out, int share = 1) {
-  double best = -1.0;
+                     int* nc_out, int share = 1, int occ = 0, int sms = 0) {
+  double best = -1.0, best_plain = -1.0;
   for (int cs = 1; cs <= 16 && cs <= upt && cs <= max_cs; ++cs) {
     if (want > 0 && cs != want) continue;
     const int ncmax = cc.max_clusters[cs] / share;
@@ -1423,14 +1436,21 @@ double plan_clusters(const ClusterCaps& cc, int tiles, int upt, int want, int ma
     const int nc = std::min(tiles, ncmax);
     const int per_cluster = (tiles + nc - 1) / nc;
     const int ku = (upt + cs - 1) / cs;
-    const double cost = per_cluster * (ku + (cs > 1 ? 0.5 : 0.0));
+    const double plain = per_cluster * (ku + (cs > 1 ? 0.5 : 0.0));
+    double cost = plain;
+    if (occ > 0 && sms > 0) {
+      const double usable = std::min((double)sms / share, (double)ncmax * cs / occ);
+      const int per_sm = (int)std::ceil((double)nc * cs / usable - 1e-9);
+      cost = per_cluster * (ku * (1.0 + 0.1 * std::max(0, per_sm - 3)) + (cs > 1 ? 0.3 * cs : 0.0));
+    }
     if (best < 0.0 || cost < best - 1e-9) {
       best = cost;
+      best_plain = plain;
       *cs_out = cs;
       *nc_out = nc;
     }
   }
-  return best;
+  return best_plain;
 }
 
 // Split-K plan of one launch: stream-K over sk.ctas CTAs (cs == 0), or nc clusters of cs CTAs.
@@ -1490,8 +1510,9 @@ int make_plan(const W4Args& a, int max_ctas, Plan* out, int share = 1) {
     // B2_TUNE_CTAS_PER_SM below the kernel's occupancy caps the resident clusters likewise
     const int cps = tuning(B2_TUNE_CTAS_PER_SM);
     const int occ_share = (cps > 0 && cps < kc.occ) ? share * kc.occ / cps : share;
+    const int cocc = FUSED ? 0 : cc->occ;  // placement model for plain launches
     const double cost = plan_clusters(*cc, sk.tiles, sk.upt, tuning(B2_TUNE_W4_CLUSTER), max_cs,
-                                      &cs, &nc, occ_share);
+                                      &cs, &nc, occ_share, cocc, di.sm_count);
     // stream-K: even units per CTA, plus the tail of the CTAs that finish a shared tile
     const long long per_cta = (sk.total + sk.ctas - 1) / sk.ctas;
     const double sk_cost = (double)per_cta + ((sk.total % sk.upt == 0 && sk.ctas <= sk.tiles &&
