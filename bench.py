@@ -343,7 +343,7 @@ def measure_gemm(lib, capi, ws, name, kind, M, K, N, G, steps, warmup, peak, l2)
     to exceed 3x L2 (so every launch reads HBM), timed by replaying the graph."""
     import torch
 
-    w4 = kind in ("w4", "w4p")
+    w4 = kind in ("w4", "w4p", "w4n")
     wbytes = K * N // 2 if w4 else 2 * N * K
     nb = w4_bytes(M, K, N, G) if w4 else f16_bytes(M, K, N)
     copies = max(1, int(3 * l2 // wbytes) + 1)
@@ -369,7 +369,11 @@ def measure_gemm(lib, capi, ws, name, kind, M, K, N, G, steps, warmup, peak, l2)
             calls.append((torch.randn(N, K, device="cuda", generator=g) * 0.02).half(),)
 
     def launch(t, sp):
-        if kind == "w4p":
+        if kind == "w4n":  # the entry point that allocates nothing (fixed scratch in the library)
+            qw, qz, sc = t
+            rc = lib.b2_w4_gemm_noalloc(x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(),
+                                        y.data_ptr(), M, K, N, G, sp)
+        elif kind == "w4p":
             rc = lib.b2_w4_gemm_packed(x.data_ptr(), t[0].data_ptr(), y.data_ptr(), M, K, N, G,
                                        ws.data_ptr(), ws.numel(), sp)
         elif kind == "w4":
@@ -648,6 +652,11 @@ SWEEP = (
     + [(f"drafter_{nm}_M{M}", "f16", M, K, N, 0) for M in (1, 7, 8)
        for nm, (N, K) in DRAFTER.items()]
     + [("check_w4_G32", "w4", 8, 5120, 1024, 32)]
+    # the same shapes through b2_w4_gemm_noalloc (no workspace argument)
+    + [("cfg0_noalloc", "w4n", 7, 4096, 4096, 128)]
+    + [(f"cfg2_{nm}_M8_noalloc", "w4n", 8, K, N, 128)
+       for nm, (K, N) in {"qkv": (5120, 8192), "o_proj": (6144, 5120), "gate_up": (5120, 34816),
+                          "down": (17408, 5120)}.items()]
     # weights repacked at load time (b2_w4_repack): the same shapes through b2_w4_gemm_packed
     + [("cfg0_packed", "w4p", 7, 4096, 4096, 128)]
     + [(f"cfg2_{nm}_M8_packed", "w4p", 8, K, N, 128)
@@ -685,7 +694,7 @@ def run_sweep(args):
         if args.only and not any(o in w[0] for o in args.only.split(",")):
             continue
         r = measure_gemm(lib, capi, ws, *w, args.steps, args.warmup, peak, l2)
-        if w[1] in ("w4", "w4p"):
+        if w[1] in ("w4", "w4p", "w4n"):
             r["plan"] = capi.w4_plan(w[2], w[3], w[4], w[5])
         print(json.dumps(r), flush=True)
         torch.cuda.empty_cache()
@@ -863,6 +872,8 @@ def main():
                     help="per-unit timeline of one W4 cluster-kernel launch (trace build: "
                          "python mi50-vllm-lab_b200/builder.py --trace)")
     ap.add_argument("--trace-units", action="store_true", help="with --trace: the raw stamps too")
+    ap.add_argument("--trace-fused", default="", metavar="K,N",
+                    help="under torchrun: phase timeline of the fused GEMM + all-reduce (trace build)")
     ap.add_argument("--norm-epilogue", action="store_true",
                     help="row-parallel W4 layer + residual add + RMSNorm: fused vs separate, 1 GPU")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
@@ -874,6 +885,16 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.trace_fused:
+        import __graft_entry__ as entry
+
+        entry.load_package()
+        from mi50_vllm_lab_b200 import trace_fused
+
+        out = trace_fused.main([args.trace_fused] + list(args.tune))
+        if out is not None:
+            print(json.dumps(out))
+        return
     if args.impl == "reference":
         run_reference(args)
     elif args.trace:

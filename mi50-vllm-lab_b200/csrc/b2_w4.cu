@@ -866,11 +866,18 @@ struct CfgC {
 // Timeline trace (builds with -DB2_TRACE only; the library proper compiles none of it): CTA 0 of
 // a cluster-kernel launch stamps the global timer per unit at the producer's issue (event 0), its
 // wait for a free stage (1), consumer warp 0's wait for the data (2) and its end of the unit (3),
-// and per tile at the start of the reduction (4); every CTA records its start, end and SM.
+// and per tile at the start of the reduction (4). Every CTA records [0] its start, [1] its end,
+// [2] its SM, [3] the end of its last tile's units, [4] the end of that tile's cluster reduction
+// (and, fused, of its sends to the ranks), [5] / [6] the start / end of the fused exchange's
+// second phase (gathering the ranks' partials), [7] the end of the wait for the previous grid.
 #ifdef B2_TRACE
-constexpr int kTraceUnits = 4096, kTraceCtas = 4096;
+constexpr int kTraceUnits = 4096, kTraceCtas = 4096, kTraceCtaWords = 8;
 __device__ unsigned long long g_trace_units[5][kTraceUnits];
-__device__ unsigned long long g_trace_ctas[kTraceCtas][3];
+__device__ unsigned long long g_trace_ctas[kTraceCtas][kTraceCtaWords];
+#define B2_TRC(k)                                                                    \
+  do {                                                                               \
+    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) g_trace_ctas[blockIdx.x][k] = globaltimer_ns(); \
+  } while (0)
 #define B2_TR(e, j)                                                                   \
   do {                                                                                \
     if (blockIdx.x == 0 && (j) < kTraceUnits) g_trace_units[e][j] = globaltimer_ns(); \
@@ -878,6 +885,9 @@ __device__ unsigned long long g_trace_ctas[kTraceCtas][3];
 #else
 #define B2_TR(e, j) \
   do {              \
+  } while (0)
+#define B2_TRC(k) \
+  do {            \
   } while (0)
 #endif
 
@@ -1022,6 +1032,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
 
   // ------------------------------------------------------------------ consumer warps
   grid_dep_wait();
+  B2_TRC(7);
   if (FUSED && threadIdx.x == 0) *s_gen = ar_begin(ar);
   named_bar_sync(1, kWarps * 32);
   const LaneGeo L(warp, lane, p.M);
@@ -1058,6 +1069,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
       if (++st == kStages) st = 0, ph ^= 1u;
     }
     if (warp == 0 && lane == 0) B2_TR(4, it);
+    B2_TRC(3);
 
     // ---------------------------------------------------------------- tile epilogue: reduce
     // Push, not pull: every CTA writes its partial tile into its send buffer arranged by the CTA
@@ -1150,6 +1162,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
         }
       }
     }
+    B2_TRC(4);
     // (d) tell every sender that my receive buffer is free again (only if it will be reused)
     if (it + 1 < ntile) {
       fence_proxy_async_smem();  // my reads precede the next copies into the buffer
@@ -1169,6 +1182,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
   }
   if constexpr (FUSED) {
     // -------------------------------------------------------------- fused all-reduce, phase 2
+    B2_TRC(5);
     const unsigned long long deadline = globaltimer_ns() + ar.timeout_ns;
     float ss[kMaxM];  // RMSNorm: this thread's sums of squares per row
 #pragma unroll
@@ -1244,6 +1258,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
         }
       }
     }
+    B2_TRC(6);
     if (p.norm) {
       float* s_norm = reinterpret_cast<float*>(smem + C::kNormOff);
       if (!norm_rstd(p, ar, e, ss, s_norm, s_flag) && tid == 0)
@@ -2116,7 +2131,7 @@ extern "C" int b2_w4_plan(int M, int K, int N, int group_size, int fused, int* p
 }
 
 #ifdef B2_TRACE
-// Copy the trace of the last traced launch to the host: units[5][4096] and ctas[4096][3] (64-bit
+// Copy the trace of the last traced launch to the host: units[5][4096] and ctas[4096][8] (64-bit
 // nanoseconds; SM ids in ctas[i][2]); entries not written are 0 or hold an earlier launch's.
 extern "C" int b2_trace_read(unsigned long long* units, unsigned long long* ctas) {
   if (cudaMemcpyFromSymbol(units, b2::g_trace_units, sizeof(b2::g_trace_units)) != cudaSuccess ||
@@ -2125,11 +2140,11 @@ extern "C" int b2_trace_read(unsigned long long* units, unsigned long long* ctas
   return B2_OK;
 }
 extern "C" int b2_trace_clear() {
-  static unsigned long long zero[5 * 4096];
+  static unsigned long long zero[4096 * 8];
+  static_assert(sizeof(zero) >= sizeof(b2::g_trace_units) && sizeof(zero) >= sizeof(b2::g_trace_ctas),
+                "one zero buffer clears both");
   if (cudaMemcpyToSymbol(b2::g_trace_units, zero, sizeof(b2::g_trace_units)) != cudaSuccess ||
-      cudaMemcpyToSymbol(b2::g_trace_ctas, zero, sizeof(zero) < sizeof(b2::g_trace_ctas)
-                                                     ? sizeof(zero) : sizeof(b2::g_trace_ctas)) !=
-          cudaSuccess)
+      cudaMemcpyToSymbol(b2::g_trace_ctas, zero, sizeof(b2::g_trace_ctas)) != cudaSuccess)
     return B2_ERR_CUDA;
   return B2_OK;
 }

@@ -18,6 +18,8 @@ import ctypes as C
 import json
 import statistics
 
+CTA_WORDS = 8  # per CTA: start, end, SM, units done, reduction done, exchange phase 2 start / end
+
 
 def main(argv=None) -> dict:
     ap = argparse.ArgumentParser()
@@ -64,14 +66,14 @@ def main(argv=None) -> dict:
     launch()
     torch.cuda.synchronize()
     units = (C.c_ulonglong * (5 * 4096))()
-    ctas = (C.c_ulonglong * (4096 * 3))()
+    ctas = (C.c_ulonglong * (4096 * CTA_WORDS))()
     capi.check(lib.b2_trace_read(units, ctas), "b2_trace_read")
     plan = capi.w4_plan(M, K, N, G)
     if plan["kernel"] != "w4c_kernel":
         return {"plan": plan, "note": "this shape does not take the cluster kernel: no trace"}
 
     n = plan["ctas"]
-    c = [(ctas[3 * i], ctas[3 * i + 1], ctas[3 * i + 2]) for i in range(n)]
+    c = [(ctas[CTA_WORDS * i], ctas[CTA_WORDS * i + 1], ctas[CTA_WORDS * i + 2]) for i in range(n)]
     t0 = min(s for s, _, _ in c)
     dur = [e - s for s, e, _ in c]
     per_sm = collections.Counter(sm for _, _, sm in c)
