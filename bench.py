@@ -803,6 +803,8 @@ def run_norm_epilogue(args):
                 # the same launch without early start, as the norm epilogue is launched
                 "gemm_ar_no_early_launch": lambda t: ops.w4gemm_ar(x, *t, h),
                 "gemm_ar_norm_fused": lambda t: ops.w4gemm_ar_rmsnorm(x, *t, h, r, w, eps),
+                # the same without the cooperative launch attribute (B2_TUNE_NORM_NO_COOP)
+                "gemm_ar_norm_fused_no_coop": lambda t: ops.w4gemm_ar_rmsnorm(x, *t, h, r, w, eps),
                 "gemm_ar_then_torch_norm": lambda t: torch_norm(ops.w4gemm_ar(x, *t, h), r),
             }
             if vllm_norm is not None:
@@ -817,6 +819,8 @@ def run_norm_epilogue(args):
                 reps = max(copies, min(64, 20 * copies)) // copies * copies
                 capi.check(lib.b2_set_tuning(3, 1 if vname == "gemm_ar_no_early_launch" else 0),
                            "b2_set_tuning")  # B2_TUNE_NO_PDL, read at launch (and capture) time
+                capi.check(lib.b2_set_tuning(9, 1 if vname == "gemm_ar_norm_fused_no_coop" else 0),
+                           "b2_set_tuning")
                 try:
                     for t in ws:
                         fn(t)
@@ -891,7 +895,9 @@ def main():
         entry.load_package()
         from mi50_vllm_lab_b200 import trace_fused
 
-        out = trace_fused.main([args.trace_fused] + list(args.tune))
+        kn = args.trace_fused.split(",")
+        out = trace_fused.main([",".join(kn[:2])] + (["--norm"] if "norm" in kn[2:] else [])
+                               + list(args.tune))
         if out is not None:
             print(json.dumps(out))
         return

@@ -300,6 +300,9 @@ int b2_w4_gemm_allreduce_emulated(b2_nvar* const* handles, int ranks, const void
                                      reduction buffers take the place of the drained stage ring,
                                      which leaves room for a fifth stage; nonzero keeps them
                                      apart (four stages)                                         */
+#define B2_TUNE_NORM_NO_COOP 9    /* nonzero: launch the stream-K kernel's fused RMSNorm (its
+                                     grid-wide barrier) without the cooperative attribute, so
+                                     that residency rests on the grid size alone                */
 int b2_set_tuning(int key, int value);
 int b2_get_tuning(int key);
 

@@ -61,45 +61,81 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Launch `kernel` on `stream`. With `early` the launch is marked for programmatic dependent
 // launch: its CTAs may start while the previous kernel on the stream is finishing, and they read
 // nothing that kernel writes before grid_dep_wait(). B2_TUNE_NO_PDL != 0 turns this off.
+// With `cooperative` the driver guarantees that every CTA is resident at once, or refuses the
+// launch (for kernels with a grid-wide barrier).
 template <typename... KArgs, typename... Args>
-int launch_kernel(void (*kernel)(KArgs...), int grid, int block, size_t smem, cudaStream_t stream,
-                  bool early, Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3((unsigned)block);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = (early && tuning(B2_TUNE_NO_PDL) == 0) ? 1 : 0;
-  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
-  B2_CUDA_TRY(cudaGetLastError());
-  return B2_OK;
-}
-
-// The same as a launch of thread-block clusters of `cluster` CTAs along x (grid % cluster == 0).
-template <typename... KArgs, typename... Args>
-int launch_kernel_clusters(void (*kernel)(KArgs...), int grid, int cluster, int block, size_t smem,
-                           cudaStream_t stream, bool early, Args&&... args) {
+int launch_kernel_ex(void (*kernel)(KArgs...), int grid, int block, size_t smem,
+                     cudaStream_t stream, bool early, bool cooperative, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);
   cfg.blockDim = dim3((unsigned)block);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = (unsigned)cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  int n = 0;
+  if (cooperative) {
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n].val.cooperative = 1;
+    ++n;
+  }
+  if (early && tuning(B2_TUNE_NO_PDL) == 0) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = (early && tuning(B2_TUNE_NO_PDL) == 0) ? 2 : 1;
+  cfg.numAttrs = n;
   B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
   B2_CUDA_TRY(cudaGetLastError());
   return B2_OK;
+}
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kernel)(KArgs...), int grid, int block, size_t smem, cudaStream_t stream,
+                  bool early, Args&&... args) {
+  return launch_kernel_ex(kernel, grid, block, smem, stream, early, false,
+                          std::forward<Args>(args)...);
+}
+
+// A launch of thread-block clusters of `cluster` CTAs along x (grid % cluster == 0). With
+// `cooperative` the driver guarantees that every CTA is resident at once, or refuses the launch
+// (for kernels with a grid-wide barrier).
+template <typename... KArgs, typename... Args>
+int launch_kernel_clusters_ex(void (*kernel)(KArgs...), int grid, int cluster, int block,
+                              size_t smem, cudaStream_t stream, bool early, bool cooperative,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((unsigned)block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[3];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeClusterDimension;
+  attr[n].val.clusterDim.x = (unsigned)cluster;
+  attr[n].val.clusterDim.y = 1;
+  attr[n].val.clusterDim.z = 1;
+  ++n;
+  if (cooperative) {
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n].val.cooperative = 1;
+    ++n;
+  }
+  if (early && tuning(B2_TUNE_NO_PDL) == 0) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  B2_CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+  B2_CUDA_TRY(cudaGetLastError());
+  return B2_OK;
+}
+template <typename... KArgs, typename... Args>
+int launch_kernel_clusters(void (*kernel)(KArgs...), int grid, int cluster, int block, size_t smem,
+                           cudaStream_t stream, bool early, Args&&... args) {
+  return launch_kernel_clusters_ex(kernel, grid, cluster, block, smem, stream, early, false,
+                                   std::forward<Args>(args)...);
 }
 
 }  // namespace b2

@@ -101,6 +101,7 @@ struct W4Args {
   const __half* nw;  // [N] norm weight
   __half* res;       // [M, N] residual: read, then overwritten with the sum
   float* npart;      // [grid][kMaxM] per-CTA sums of squares (workspace)
+  int norm_v16;      // y, res and nw all 16-byte aligned: the last cluster moves 16-byte vectors
   // weights repacked at load time (b2_w4_repack), or null: unit (tile, ku) is pk_unit contiguous
   // bytes at pk + (tile * K / 128 + ku) * pk_unit holding exactly the stage's shared-memory image:
   // its qw block (8 KB, already swizzled), then its scale rows, then its zero rows
@@ -493,6 +494,197 @@ __device__ __forceinline__ bool norm_rstd(const W4Args& p, const ArView& ar, uin
   return ok;
 }
 
+// Timeline trace (builds with -DB2_TRACE only; the library proper compiles none of it): CTA 0 of
+// a cluster-kernel launch stamps the global timer per unit at the producer's issue (event 0), its
+// wait for a free stage (1), consumer warp 0's wait for the data (2) and its end of the unit (3),
+// and per tile at the start of the reduction (4). Every CTA records [0] its start, [1] its end,
+// [2] its SM, [3] the end of its last tile's units, [4] the end of that tile's cluster reduction
+// (and, fused, of its sends to the ranks), [5] / [6] the start / end of the fused exchange's
+// second phase (gathering the ranks' partials), [7] the end of the wait for the previous grid;
+// RMSNorm launches: [8] its row sums sent to the cluster leader, [9] (leader) every CTA's sums in,
+// [10] (leader) past the grid-wide barrier, [11] rstd received.
+#ifdef B2_TRACE
+constexpr int kTraceUnits = 4096, kTraceCtas = 4096, kTraceCtaWords = 12;
+__device__ unsigned long long g_trace_units[5][kTraceUnits];
+__device__ unsigned long long g_trace_ctas[kTraceCtas][kTraceCtaWords];
+#define B2_TRC(k)                                                                    \
+  do {                                                                               \
+    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) g_trace_ctas[blockIdx.x][k] = globaltimer_ns(); \
+  } while (0)
+#define B2_TR(e, j)                                                                   \
+  do {                                                                                \
+    if (blockIdx.x == 0 && (j) < kTraceUnits) g_trace_units[e][j] = globaltimer_ns(); \
+  } while (0)
+#else
+#define B2_TR(e, j) \
+  do {              \
+  } while (0)
+#define B2_TRC(k) \
+  do {            \
+  } while (0)
+#endif
+
+// The last cluster's share of the final RMSNorm step over all M x N elements, in vectors V of
+// fp16 (uint4: 8, uint2: 4; N is a multiple of 8, so a vector never crosses a row): each thread
+// issues the loads of up to 4 vectors of y, residual and weight before it uses any, so its share
+// costs about one round trip to L2 instead of one per vector.
+template <typename V>
+__device__ __forceinline__ void norm_finish_all(const W4Args& p, const float* s_rstd, int crank,
+                                                int CS) {
+  constexpr int kH = (int)(sizeof(V) / 2);
+  const int per = p.M * p.N / kH, stride = CS * kWarps * 32;
+  for (int i0 = crank * kWarps * 32 + (int)threadIdx.x; i0 < per; i0 += 4 * stride) {
+    V yv[4], rv[4], wv[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = i0 + j * stride;
+      if (i < per) {
+        const int m = (i * kH) / p.N, n = i * kH - m * p.N;
+        const size_t o = (size_t)m * p.N + n;
+        yv[j] = __ldcg(reinterpret_cast<const V*>(p.y + o));
+        rv[j] = __ldcg(reinterpret_cast<const V*>(p.res + o));
+        wv[j] = __ldg(reinterpret_cast<const V*>(p.nw + n));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = i0 + j * stride;
+      if (i >= per) continue;
+      const int m = (i * kH) / p.N, n = i * kH - m * p.N;
+      const size_t o = (size_t)m * p.N + n;
+      const __half* yh = reinterpret_cast<const __half*>(&yv[j]);
+      __half* rh = reinterpret_cast<__half*>(&rv[j]);
+      const __half* wh = reinterpret_cast<const __half*>(&wv[j]);
+      V ov;
+      __half* oh = reinterpret_cast<__half*>(&ov);
+      const float rstd = s_rstd[m];
+#pragma unroll
+      for (int k = 0; k < kH; ++k) {
+        const float x = norm_x(yh[k], rh[k]);
+        rh[k] = __float2half_rn(x);
+        oh[k] = norm_out(x, rstd, wh[k]);
+      }
+      *reinterpret_cast<V*>(p.res + o) = rv[j];
+      *reinterpret_cast<V*>(p.y + o) = ov;
+    }
+  }
+}
+
+// The cluster kernel's RMSNorm, without a grid-wide barrier. (1) Each CTA adds its threads' row
+// sums (shuffle tree, warps in order) and writes them into its cluster leader's shared memory
+// (distributed shared memory, slot crank), then arrives on the leader's norm_bar. (2) The leader
+// adds the CS slots in rank order, writes the cluster's sums to the workspace and counts its
+// cluster in the handle's header (a release: its cluster's y stores and sums are ordered before).
+// Every leader but the last tells its CTAs that they are done. (3) The last leader (whose counter
+// update acquires every other cluster's) adds the NC cluster sums in cluster order - the same
+// order on every rank, so every rank computes the same rstd bit for bit - advances the handle's
+// generation (every cluster has finished reading its slots; these launches skip ar_finish) and
+// sends rstd to its CTAs, which then finish every element of y: x = y + residual, residual <-
+// fp16(x), y <- fp16(fp16(x * rstd) * weight). No CTA waits for another cluster, so the launch
+// needs no co-residency (it may start early). Every wait is bounded; the leader always tells its
+// CTAs, so none of them waits in vain. Returns false if a wait gave up.
+__device__ __forceinline__ bool norm_finish_cluster(const W4Args& p, const ArView& ar, uint32_t e,
+                                                    const float (&ss)[kMaxM], float* s_norm,
+                                                    uint64_t* norm_bar, uint64_t* rstd_bar,
+                                                    volatile int* s_flag, volatile int* s_abort,
+                                                    int crank, int CS, int cid, int NC) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float* s_rstd = s_norm + kWarps * kMaxM;   // [kMaxM]
+  float* s_fin = s_rstd + kMaxM;             // [0]: nonzero in the CTAs of the last cluster
+  float* s_gather = s_fin + kMaxM;           // [16][kMaxM] (leader)
+  float* s_part = s_gather + 16 * kMaxM;     // [16][kMaxM] (leader)
+  volatile int* s_last = reinterpret_cast<volatile int*>(s_part + 16 * kMaxM);
+#pragma unroll
+  for (int m = 0; m < kMaxM; ++m) {
+    float v = ss[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) s_norm[warp * kMaxM + m] = v;
+  }
+  named_bar_sync(1, kWarps * 32);
+  if (tid < kMaxM) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) v += s_norm[w * kMaxM + tid];
+    st_dsmem_f32(mapa_shared(smem_u32(s_gather + crank * kMaxM + tid), 0u), v);
+  }
+  named_bar_sync(1, kWarps * 32);  // (also orders every thread's y stores before the arrival)
+  if (tid == 0) {
+    fence_acq_rel_cluster();
+    mbar_arrive_remote(mapa_shared(smem_u32(norm_bar), 0u));
+  }
+  B2_TRC(8);
+  bool ok = true;
+  if (crank == 0) {
+    if (tid == 0) *s_flag = mbar_wait_cluster(norm_bar, 0u, s_abort) ? 1 : 0;
+    B2_TRC(9);
+    named_bar_sync(1, kWarps * 32);
+    ok = *s_flag != 0;
+    if (tid < kMaxM) {
+      float v = 0.f;
+      for (int q = 0; q < CS; ++q) v += s_gather[q * kMaxM + tid];
+      p.npart[(size_t)cid * kMaxM + tid] = v;
+    }
+    named_bar_sync(1, kWarps * 32);
+    if (tid == 0) {
+      ArHeader* h = ar_header(ar);
+      __threadfence();  // the cluster's y stores and sums before its count
+      const bool last = atomicAdd(&h->norm_count, 1u) == (unsigned)NC - 1u;
+      if (last) {
+        __threadfence();  // every other cluster's stores after their counts
+        atomicExch(&h->norm_count, 0u);
+      }
+      *s_last = last ? 1 : 0;
+    }
+    named_bar_sync(1, kWarps * 32);
+    const bool last = *s_last != 0;
+    B2_TRC(10);
+    if (last) {
+      {
+        const int m = tid & (kMaxM - 1), j = tid / kMaxM;  // 16 threads per row
+        float v = 0.f;
+        for (int b = j; b < NC; b += 16) v += __ldcg(p.npart + (size_t)b * kMaxM + m);
+        s_part[j * kMaxM + m] = v;
+      }
+      named_bar_sync(1, kWarps * 32);
+      if (tid == 0) {  // in place of ar_finish (read by this GPU's next launch: gpu scope)
+        __threadfence();
+        atomicExch(&ar_header(ar)->gen, e);
+      }
+    }
+    if (last && tid < kMaxM) {
+      float v = 0.f;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v += s_part[j * kMaxM + tid];
+      s_rstd[tid] = rsqrtf(v / (float)p.N + p.eps);  // (this CTA's own copy, read below)
+    }
+    named_bar_sync(1, kWarps * 32);
+    // to every CTA of the cluster at once: thread q * kMaxM + m stores row m's rstd into CTA q,
+    // thread q the "finish" word, then (after the CTA barrier) arrives on CTA q's rstd_bar
+    {
+      const int q = tid / kMaxM, m = tid - q * kMaxM;
+      if (q < CS && q > 0 && last) st_dsmem_f32(mapa_shared(smem_u32(s_rstd + m), (uint32_t)q), s_rstd[m]);
+      if (tid < CS) st_dsmem_f32(mapa_shared(smem_u32(s_fin), (uint32_t)tid), last ? 1.f : 0.f);
+    }
+    named_bar_sync(1, kWarps * 32);
+    if (tid < CS) {
+      fence_acq_rel_cluster();
+      mbar_arrive_remote(mapa_shared(smem_u32(rstd_bar), (uint32_t)tid));
+    }
+  }
+  if (tid == 0) *s_flag = mbar_wait_cluster(rstd_bar, 0u, s_abort) ? 1 : 0;
+  B2_TRC(11);
+  named_bar_sync(1, kWarps * 32);
+  ok = ok && *s_flag != 0;
+  if (s_fin[0] != 0.f) {  // the last cluster finishes every element
+    if (p.norm_v16)
+      norm_finish_all<uint4>(p, s_rstd, crank, CS);
+    else
+      norm_finish_all<uint2>(p, s_rstd, crank, CS);
+  }
+  return ok;
+}
+
 // A = (q - z) in fp16 (exact, see dequant_word) against B = x; the fp32 sum of each quantization
 // group is scaled once: acc += s * sum. Every weight is dequantized once per CTA and used for all
 // M rows.
@@ -855,41 +1047,19 @@ struct CfgC {
   static constexpr int kRecvOff = kSendOff + kMaxM * kTileN * 4;
   static constexpr int kRecvBytes = kMaxM * (kTileN + 16) * 4;
   static constexpr int kBarOff = A ? kRingEnd : kRecvOff + kRecvBytes;
-  static constexpr int kNormOff = align128(kBarOff + (2 * kStages + 3) * 8 + 32);
-  static constexpr int kSmem = 1024 + kNormOff + kNormFloats * 4;
+  // full[S], empty[S], red_full, red_empty, pub_bar, norm_bar, rstd_bar
+  static constexpr int kNormOff = align128(kBarOff + (2 * kStages + 5) * 8 + 32);
+  // RMSNorm epilogue (fused launches): warp row sums [kWarps][kMaxM], rstd [kMaxM], the "finish"
+  // word [kMaxM], the cluster's CTA row sums gathered at its leader [16][kMaxM], the leader's
+  // partial sums [16][kMaxM], the leader's "last cluster" word [kMaxM]
+  static constexpr int kNormClusterFloats = (kWarps + 2) * kMaxM + 2 * 16 * kMaxM + kMaxM;
+  static constexpr int kSmem = 1024 + kNormOff + (A ? 0 : kNormClusterFloats * 4);
   static_assert(kXOff % 1024 == 0 && kXBytes % 1024 == 0, "swizzled boxes need 1024 B");
   static_assert(kScOff % 128 == 0 && kQzOff % 128 == 0 && kSendOff % 128 == 0 &&
                     kRecvOff % 128 == 0, "alignment");
   static_assert(!A || kRecvOff + kRecvBytes <= kXOff, "aliased buffers lie inside the qw ring");
 };
 
-// Timeline trace (builds with -DB2_TRACE only; the library proper compiles none of it): CTA 0 of
-// a cluster-kernel launch stamps the global timer per unit at the producer's issue (event 0), its
-// wait for a free stage (1), consumer warp 0's wait for the data (2) and its end of the unit (3),
-// and per tile at the start of the reduction (4). Every CTA records [0] its start, [1] its end,
-// [2] its SM, [3] the end of its last tile's units, [4] the end of that tile's cluster reduction
-// (and, fused, of its sends to the ranks), [5] / [6] the start / end of the fused exchange's
-// second phase (gathering the ranks' partials), [7] the end of the wait for the previous grid.
-#ifdef B2_TRACE
-constexpr int kTraceUnits = 4096, kTraceCtas = 4096, kTraceCtaWords = 8;
-__device__ unsigned long long g_trace_units[5][kTraceUnits];
-__device__ unsigned long long g_trace_ctas[kTraceCtas][kTraceCtaWords];
-#define B2_TRC(k)                                                                    \
-  do {                                                                               \
-    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) g_trace_ctas[blockIdx.x][k] = globaltimer_ns(); \
-  } while (0)
-#define B2_TR(e, j)                                                                   \
-  do {                                                                                \
-    if (blockIdx.x == 0 && (j) < kTraceUnits) g_trace_units[e][j] = globaltimer_ns(); \
-  } while (0)
-#else
-#define B2_TR(e, j) \
-  do {              \
-  } while (0)
-#define B2_TRC(k) \
-  do {            \
-  } while (0)
-#endif
 
 template <int GP, bool FUSED, bool A = false>
 __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtensorMap& tm_sc,
@@ -912,7 +1082,9 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
   uint64_t* red_full = empty + kStages;  // the CS slices of the tile have landed in s_recv
   uint64_t* red_empty = red_full + 1;    // every receiver has added up my previous tile
   uint64_t* pub_bar = red_empty + 1;     // (CTA 0, fp32 flag exchange) every CTA pushed its slice
-  volatile int* s_abort = reinterpret_cast<volatile int*>(pub_bar + 1);
+  uint64_t* norm_bar = pub_bar + 1;      // (leader, RMSNorm) every CTA's row sums have landed
+  uint64_t* rstd_bar = norm_bar + 1;     // (RMSNorm) the leader has sent this CTA the rstd
+  volatile int* s_abort = reinterpret_cast<volatile int*>(rstd_bar + 1);
   volatile int* s_flag = s_abort + 1;
   volatile uint32_t* s_gen = reinterpret_cast<volatile uint32_t*>(s_abort + 2);
 
@@ -937,6 +1109,8 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
     mbar_init(red_full, 1);  // my own expect-tx; the senders' copies complete the bytes
     mbar_init(red_empty, CS);
     mbar_init(pub_bar, CS);
+    mbar_init(norm_bar, CS);
+    mbar_init(rstd_bar, 1);
     *s_abort = 0;
     *s_flag = 0;
     mbar_fence_init();
@@ -1261,18 +1435,13 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
     B2_TRC(6);
     if (p.norm) {
       float* s_norm = reinterpret_cast<float*>(smem + C::kNormOff);
-      if (!norm_rstd(p, ar, e, ss, s_norm, s_flag) && tid == 0)
+      if (!norm_finish_cluster(p, ar, e, ss, s_norm, norm_bar, rstd_bar, s_flag, s_abort, crank,
+                               CS, cid, NC) &&
+          tid == 0)
         atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
-      for (int it = 0; it < ntile; ++it) {
-        const int tile = cid + it * NC;
-        for (int idx = tid; idx < p.M * W; idx += kWarps * 32) {
-          const int m = idx / W, n = tile * kTileN + c0 + (idx - m * W);
-          if (n < p.N) norm_finish1(p, m, n, s_norm[kWarps * kMaxM + m]);
-        }
-      }
     }
     named_bar_sync(1, kWarps * 32);
-    if (tid == 0) ar_finish(ar, e);
+    if (tid == 0 && !p.norm) ar_finish(ar, e);  // (norm launches advanced the generation above)
   }
   // Before this CTA exits, no peer may still write into its shared memory or arrive on its
   // barriers, and its own outgoing copies must be done reading its send buffer. On the normal
@@ -1290,6 +1459,12 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
       *no_abort = 0;
       if (FUSED && !p.ll && crank == 0)
         mbar_wait_cluster(pub_bar, (uint32_t)((ntile - 1) & 1), no_abort);
+      if (FUSED && p.norm) {  // the leader's rstd here, and (leader) every CTA's row sums
+        *no_abort = 0;
+        mbar_wait_cluster(rstd_bar, 0u, no_abort);
+        *no_abort = 0;
+        if (crank == 0) mbar_wait_cluster(norm_bar, 0u, no_abort);
+      }
     }
     if (tid < CS) bulk_wait_read_all();
     named_bar_sync(1, kWarps * 32);
@@ -1584,8 +1759,14 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
                                   CfgC<GP>::kSmem, stream, early, m_qw, m_sc, m_qz, m_x, a, view);
   }
   a.cl_size = a.cl_count = 0;
-  return launch_kernel(w4_kernel<GP, FUSED>, pl.sk.ctas, kThreads, C::kSmem, stream, early, m_qw,
-                       m_sc, m_qz, m_x, a, view);
+  // The stream-K kernel's RMSNorm epilogue has a grid-wide barrier: every CTA must be resident at
+  // once. A cooperative launch gets that guarantee from the driver (or is refused), and it starts
+  // only after the previous kernel: launched early, a grid's first CTAs take whatever slots the
+  // previous grid leaves free and the rest may not fit beside them.
+  const bool barrier = FUSED && a.norm != 0;
+  return launch_kernel_ex(w4_kernel<GP, FUSED>, pl.sk.ctas, kThreads, C::kSmem, stream,
+                          early && !barrier, barrier && !tuning(B2_TUNE_NORM_NO_COOP), m_qw, m_sc,
+                          m_qz, m_x, a, view);
 }
 
 // The plan of a launch for the group size in args.G.
@@ -1660,6 +1841,7 @@ W4Args make_args(const void* a, void* y, int M, int K, int N, int G, void* ws) {
   r.nw = nullptr;
   r.res = nullptr;
   r.npart = nullptr;
+  r.norm_v16 = 0;
   r.pk = nullptr;
   r.pk_unit = 0;
   return r;
@@ -1935,6 +2117,7 @@ int fused_args(b2_nvar* h, const void* a, const void* qw, const void* qz, const 
     args.res = static_cast<__half*>(residual);
     args.nw = static_cast<const __half*>(nw);
     args.npart = reinterpret_cast<float*>(static_cast<char*>(ws) + ws_norm_offset());
+    args.norm_v16 = aligned16(y) && aligned16(residual) && aligned16(nw) ? 1 : 0;
   }
   *out = args;
   return B2_OK;
@@ -1951,14 +2134,10 @@ int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* q
   if (rc) return rc;
   // Early launch is safe here too: the generation is read after griddepcontrol.wait, and a
   // dependent grid starts only once every CTA of this one is resident, so none of the CTAs that
-  // wait for peers in the second phase can be held back.
-  // The RMSNorm epilogue's grid-wide barrier needs every CTA resident at once, so that launch
-  // starts only after the previous kernel has finished. Launched early, a grid's first clusters
-  // take whatever slots the previous grid leaves free; measured on B200 with 40 clusters of 12
-  // CTAs (42 fit an idle GPU), fewer than 40 could then be resident together and back-to-back
-  // launches ran their barrier into the timeout. A kernel after this one may still start early:
-  // by then every CTA of this grid is resident.
-  return dispatch<true>(args, qw, qz, sc, &v, stream, /*early=*/!args.norm);
+  // wait for peers in the second phase can be held back. (The cluster kernel's RMSNorm needs no
+  // co-residency either: its last cluster finishes the rows. The stream-K kernel's, with a
+  // grid-wide barrier, is launched without early start; see launch.)
+  return dispatch<true>(args, qw, qz, sc, &v, stream, /*early=*/true);
 }
 
 // `R` ranks of one group in one cooperative launch on this GPU (grid.y = rank). Every rank gets
@@ -2131,7 +2310,7 @@ extern "C" int b2_w4_plan(int M, int K, int N, int group_size, int fused, int* p
 }
 
 #ifdef B2_TRACE
-// Copy the trace of the last traced launch to the host: units[5][4096] and ctas[4096][8] (64-bit
+// Copy the trace of the last traced launch to the host: units[5][4096] and ctas[4096][12] (64-bit
 // nanoseconds; SM ids in ctas[i][2]); entries not written are 0 or hold an earlier launch's.
 extern "C" int b2_trace_read(unsigned long long* units, unsigned long long* ctas) {
   if (cudaMemcpyFromSymbol(units, b2::g_trace_units, sizeof(b2::g_trace_units)) != cudaSuccess ||
@@ -2140,7 +2319,7 @@ extern "C" int b2_trace_read(unsigned long long* units, unsigned long long* ctas
   return B2_OK;
 }
 extern "C" int b2_trace_clear() {
-  static unsigned long long zero[4096 * 8];
+  static unsigned long long zero[4096 * 12];
   static_assert(sizeof(zero) >= sizeof(b2::g_trace_units) && sizeof(zero) >= sizeof(b2::g_trace_ctas),
                 "one zero buffer clears both");
   if (cudaMemcpyToSymbol(b2::g_trace_units, zero, sizeof(b2::g_trace_units)) != cudaSuccess ||

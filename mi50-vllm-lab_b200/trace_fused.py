@@ -2,7 +2,7 @@
 trace build (builder.py --trace). One process per GPU:
 
     python -m torch.distributed.run --nnodes=1 --nproc-per-node P --master-addr 127.0.0.1 \\
-        --master-port 29541 bench.py --trace-fused K,N [--tune KEY=VALUE ...]
+        --master-port 29541 bench.py --trace-fused K,N[,norm] [--tune KEY=VALUE ...]
 
 Each rank builds an all-reduce handle through the C ABI (IPC handles exchanged over gloo), runs a
 chain of `chain` fused launches back to back (the exchange keeps the ranks in step, as inside a
@@ -21,7 +21,7 @@ import json
 import os
 import statistics
 
-CTA_WORDS = 8
+CTA_WORDS = 12
 
 
 def main(argv) -> dict | None:
@@ -31,7 +31,8 @@ def main(argv) -> dict | None:
     from . import builder, capi
 
     K, N = (int(v) for v in argv[0].split(","))
-    tune = argv[1:]
+    norm = "--norm" in argv[1:]
+    tune = [a for a in argv[1:] if a != "--norm"]
     M, G, chain = 8, 128, 40
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -60,10 +61,18 @@ def main(argv) -> dict | None:
     qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), device="cuda", dtype=torch.int32, generator=g)
     sc = (torch.rand(K // G, N, device="cuda", generator=g) * 0.015 + 0.005).half()
     y = torch.empty(M, N, dtype=torch.float16, device="cuda")
+    res = torch.randn(M, N, device="cuda", generator=g).half()
+    nw = torch.ones(N, device="cuda", dtype=torch.float16)
     ws = torch.zeros(lib.b2_workspace_bytes(local), dtype=torch.uint8, device="cuda")
     sp = torch.cuda.current_stream().cuda_stream
 
     def launch():
+        if norm:
+            capi.check(lib.b2_w4_gemm_allreduce_rmsnorm(
+                h, x.data_ptr(), qw.data_ptr(), qz.data_ptr(), sc.data_ptr(), res.data_ptr(),
+                nw.data_ptr(), 1e-6, y.data_ptr(), M, K, N, G, ws.data_ptr(), ws.numel(), sp),
+                "b2_w4_gemm_allreduce_rmsnorm")
+            return
         capi.check(lib.b2_w4_gemm_allreduce(h, x.data_ptr(), qw.data_ptr(), qz.data_ptr(),
                                             sc.data_ptr(), y.data_ptr(), M, K, N, G,
                                             ws.data_ptr(), ws.numel(), sp), "b2_w4_gemm_allreduce")
@@ -107,12 +116,32 @@ def main(argv) -> dict | None:
         "tail_ns": med([r[1] - r[6] for r in rows]),
         "start_spread_ns": max(r[0] for r in rows) - t0,
     }
+    if norm:
+        lead = [rows[i] for i in range(0, n, plan["cluster"])]
+        mine.update({
+            "norm_sums_sent_ns": med([r[8] - r[6] for r in rows]),
+            "norm_leader_gathered_ns": med([r[9] - r[8] for r in lead]),
+            "norm_leader_grid_barrier_ns": med([r[10] - r[9] for r in lead]),
+            "norm_rstd_received_ns": med([r[11] - r[8] for r in rows]),
+            "norm_finish_and_exit_ns": med([r[1] - r[11] for r in rows]),
+        })
+        # the last cluster (its leader counted last) finishes every row
+        cs = plan["cluster"]
+        li = max(range(0, n, cs), key=lambda i: rows[i][10])
+        last = rows[li:li + cs]
+        mine.update({
+            "last_cluster_units_end_to_count_ns": rows[li][10] - max(r[3] for r in last),
+            "last_cluster_count_to_rstd_ns": med([r[11] for r in last]) - rows[li][10],
+            "last_cluster_finish_and_exit_ns": med([r[1] - r[11] for r in last]),
+            "last_cluster_end_minus_kernel_others_end_ns":
+                max(r[1] for r in last) - max(r[1] for i, r in enumerate(rows) if not li <= i < li + cs),
+        })
     every = [None] * world
     dist.all_gather_object(every, mine)
     capi.check(lib.b2_nvar_destroy(h), "b2_nvar_destroy")
     dist.barrier()
     dist.destroy_process_group()
     if rank == 0:
-        return {"world": world, "shape": {"M": M, "K": K, "N": N, "G": G}, "plan": plan,
-                "tune": tune, "ranks": every}
+        return {"world": world, "shape": {"M": M, "K": K, "N": N, "G": G}, "norm": norm,
+                "plan": plan, "tune": tune, "ranks": every}
     return None

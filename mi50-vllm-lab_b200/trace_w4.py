@@ -18,7 +18,7 @@ import ctypes as C
 import json
 import statistics
 
-CTA_WORDS = 8  # per CTA: start, end, SM, units done, reduction done, exchange phase 2 start / end
+CTA_WORDS = 12  # per CTA: start, end, SM, units done, reduction done, exchange phase 2, ...
 
 
 def main(argv=None) -> dict:
