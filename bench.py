@@ -245,9 +245,15 @@ def layer_shapes(P: int) -> dict:
 
 class DecodeModel:
     """Random-initialised weights of one rank's shard of config 4 and the step that runs them
-    through torch.ops.gfx906_skinny (the operators vLLM calls)."""
+    through torch.ops.gfx906_skinny (the operators vLLM calls).
 
-    def __init__(self, ops, P: int, rank: int, ar, seed: int = 4000):
+    `norm` adds the decoder layer's two residual-add + RMSNorm steps, which vLLM runs on the
+    all-reduced outputs of o_proj and down_proj (fused_add_rms_norm): "fused" in the GEMM's
+    epilogue (w4gemm_ar_rmsnorm; at TP=1 through a one-rank handle `h1`), "unfused" as a separate
+    step after it (the torch restatement of vLLM's reference code, vllm/ir/ops/layernorm.py:48-58).
+    The residual stream restarts from the step's input every step."""
+
+    def __init__(self, ops, P: int, rank: int, ar, seed: int = 4000, norm=None, h1=None):
         import torch
 
         c = CFG4
@@ -271,9 +277,25 @@ class DecodeModel:
         # attention and the activation are not part of this path)
         self.a_o = (torch.randn(M, c["o_in"] // P, device="cuda", generator=g) * 0.05).half()
         self.a_d = (torch.randn(M, c["inter"] // P, device="cuda", generator=g) * 0.05).half()
+        self.norm, self.h1 = norm, h1
+        self.res = torch.empty(M, H, device="cuda", dtype=torch.float16)
+        self.nw = [(1.0 + (torch.rand(2, H, device="cuda", generator=g) - 0.5) * 0.2).half()
+                   for _ in range(c["layers"])]
 
     def row_parallel(self, a, w):
         return self.ar.w4_gemm_all_reduce(a, *w) if self.ar else self.ops.w4gemm(a, *w, 0, 0)
+
+    def row_parallel_norm(self, a, w, nw):
+        """Row-parallel GEMM, all-reduce, then residual add + RMSNorm (fused or not)."""
+        eps = 1e-6
+        if self.norm == "fused":
+            if self.ar:
+                return self.ar.w4_gemm_all_reduce_rmsnorm(a, *w, self.res, nw, eps)
+            return self.ops.w4gemm_ar_rmsnorm(a, *w, self.h1, self.res, nw, eps)
+        y = self.row_parallel(a, w)
+        xf = y.float() + self.res.float()
+        self.res.copy_(xf.half())
+        return ((xf * (xf.pow(2).mean(dim=-1, keepdim=True) + eps).rsqrt()).half() * nw)
 
     def launch(self, kind: str, L: dict, h):
         if kind in ("o", "down"):
@@ -282,6 +304,14 @@ class DecodeModel:
 
     def step(self):
         h = self.x0
+        if self.norm:
+            self.res.copy_(self.x0)
+            for L, nw in zip(self.layers, self.nw):
+                self.launch("qkv", L, h)
+                h = self.row_parallel_norm(self.a_o, L["o"], nw[0])
+                self.launch("gate_up", L, h)
+                h = self.row_parallel_norm(self.a_d, L["down"], nw[1])
+            return self.ops.gemm(h, self.lm, 0)
         for L in self.layers:
             self.launch("qkv", L, h)
             h = self.launch("o", L, h)
@@ -474,6 +504,27 @@ def run_gpu(args):
     e2e_ms = time_steps(e2e_step, args.steps, world, stream)
     e2e_us = max_over_ranks(e2e_ms * 1e3 / args.steps, world)
 
+    # the same step with the decoder layer's two residual-add + RMSNorm steps per layer: fused
+    # into the row-parallel GEMMs' epilogue, and as separate steps after them (one graph each)
+    norms = {}
+    if P == 1:
+        name = f"/b2_bench_h1_{os.getpid()}"
+        model.h1 = ops.nvar_create(name, M * H * 8, 0, 1)
+        ops.hostar_unlink(name)
+    for mode in ("fused", "unfused"):
+        model.norm = mode
+        model.step()
+        torch.cuda.synchronize()
+        g_n, _ = capture(model.step)
+        for _ in range(args.warmup):
+            g_n.replay()
+        torch.cuda.synchronize()
+        ms = time_steps(g_n.replay, args.steps, world, stream)
+        norms[f"{mode}_us_per_step"] = round(max_over_ranks(ms * 1e3 / args.steps, world), 1)
+        del g_n
+    model.norm = None
+    norms["norms_per_step"] = 2 * c["layers"]
+
     kernels = kernel_breakdown(model, world, capi)
     status = ar.status() if ar else ops.workspace_status(False)
     peak, peak_kind = hbm_peak()
@@ -517,6 +568,7 @@ def run_gpu(args):
                          "bytes_per_launch": dom["bytes_per_launch"],
                          "traffic": recorded_traffic(dom["kernel"].split("<")[0], workload)},
             "kernels": kernels,
+            "config4_with_norms": norms,
             "gpu_launches": args.steps * (4 * c["layers"] + 1),
             "graph_equals_eager": same, "device_status": int(status),
             "clocks": clk.summary(),

@@ -428,11 +428,11 @@ __device__ __forceinline__ bool norm_rstd(const W4Args& p, const ArView& ar, uin
     __threadfence();
     if (atomicAdd(&h->norm_count, 1u) == gridDim.x - 1) {
       atomicExch(&h->norm_count, 0u);
-      st_release_sys(&h->norm_gen, e);
+      st_release_gpu(&h->norm_gen, e);  // the grid barrier is on this GPU: gpu scope
     } else {
       const unsigned long long t0 = globaltimer_ns();
       unsigned int it = 0;
-      while ((int)(ld_acquire_sys(&h->norm_gen) - e) < 0) {
+      while ((int)(ld_acquire_gpu(&h->norm_gen) - e) < 0) {
         if (++it >= kMaxSpin || ((it & 15u) == 0 && globaltimer_ns() - t0 > ar.timeout_ns)) {
           ok = false;
           break;
