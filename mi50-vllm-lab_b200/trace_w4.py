@@ -108,6 +108,15 @@ def main(argv=None) -> dict:
                  "consume_ns": med(consume), "starve_ns": med(starve),
                  "ns_per_unit": round((u[3][nu - 1] - u[2][0]) / max(1, nu - 1)) if nu > 1 else None},
     }
+    # per CTA (medians): start -> units done (3), units done -> reduction done (4), -> end (1)
+    full = [[ctas[CTA_WORDS * i + k] for k in range(CTA_WORDS)] for i in range(n)]
+    ok_rows = [r for r in full if r[3] and r[4]]
+    if ok_rows:
+        out["ctas"]["start_to_units_done_ns"] = med([r[3] - r[0] for r in ok_rows])
+        out["ctas"]["units_done_to_reduced_ns"] = med([r[4] - r[3] for r in ok_rows])
+        out["ctas"]["reduced_to_end_ns"] = med([r[1] - r[4] for r in ok_rows])
+    if nu:
+        out["cta0"]["start_to_first_issue_ns"] = u[0][0] - c[0][0]
     if a.units:
         out["cta0"]["stamps_ns"] = [[(u[e][j] - base) if u[e][j] else None for e in range(4)]
                                     for j in range(nu)]
