@@ -292,7 +292,7 @@ int b2_w4_gemm_allreduce_emulated(b2_nvar* const* handles, int ranks, const void
 #define B2_TUNE_W4_CLUSTER 5      /* cluster path: CTAs per cluster (0 = chosen per shape)      */
 #define B2_TUNE_AR_FLAGS 6        /* fused all-reduce: nonzero sends fp32 values published by
                                      per-tile flags instead of 64-bit (generation, value) words  */
-#define B2_TUNE_AR_TWO_SHOT 7     /* fused all-reduce in the cluster kernel: 0 = two-shot from 4
+#define B2_TUNE_AR_TWO_SHOT 7     /* fused all-reduce in the cluster kernel: 0 = two-shot from 8
                                      ranks up (each tile reduced at one owner rank, the result
                                      sent back), 1 = always two-shot, 2 = always one-shot        */
 #define B2_TUNE_W4_NO_ALIAS 8     /* cluster path, G >= 128, no exchange: when every cluster has

@@ -1227,6 +1227,12 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
   int st = 0;
   uint32_t ph = 0;
   bool ok = true;
+  // one rank (a one-rank handle): there is nothing to exchange, so the reduced tile is stored as
+  // y at once, with the RMSNorm's sums of squares, and the exchange's second phase is skipped
+  const bool solo = FUSED && ar.world == 1;
+  float ss1[kMaxM];
+#pragma unroll
+  for (int i = 0; i < kMaxM; ++i) ss1[i] = 0.f;
   for (int it = 0; it < ntile; ++it) {
     const int tile = cid + it * NC;
     for (int ku = k0; ku < k1; ++ku) {
@@ -1316,8 +1322,13 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
         if (q < CS) s += part[q];
       const int n = tile * kTileN + col;
       if (n < p.N) {
-        if (!FUSED) {
-          p.y[(size_t)m * p.N + n] = __float2half_rn(s);
+        if (!FUSED || solo) {
+          const __half yh = __float2half_rn(s);
+          p.y[(size_t)m * p.N + n] = yh;
+          if (FUSED && p.norm) {
+            const float x = norm_x(yh, p.res[(size_t)m * p.N + n]);
+            row_add(ss1, m, x * x);
+          }
         } else {
           // exchange layout: slice (tile, crank) is one block of M x W floats at
           // (tile * 128 + c0) * M, element idx in the order the threads produce them, so a
@@ -1347,7 +1358,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
     // completes; CTA 0 then publishes the tile with one system-scope fence (the peers' pushes
     // happen before it through their CTA barrier and cluster-scope release, which the fence's
     // cumulativity covers).
-    if (FUSED && !p.ll) {
+    if (FUSED && !p.ll && !solo) {
       named_bar_sync(1, kWarps * 32);
       if (tid == 0) mbar_arrive_remote(mapa_shared(smem_u32(pub_bar), 0u));
       if (crank == 0 && tid == 0 && mbar_wait_cluster(pub_bar, (uint32_t)(it & 1), s_abort))
@@ -1360,8 +1371,8 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
     const unsigned long long deadline = globaltimer_ns() + ar.timeout_ns;
     float ss[kMaxM];  // RMSNorm: this thread's sums of squares per row
 #pragma unroll
-    for (int i = 0; i < kMaxM; ++i) ss[i] = 0.f;
-    for (int it = 0; it < ntile; ++it) {
+    for (int i = 0; i < kMaxM; ++i) ss[i] = ss1[i];
+    for (int it = 0; it < (solo ? 0 : ntile); ++it) {
       const int tile = cid + it * NC;
       const size_t blk = ((size_t)tile * kTileN + c0) * p.M;
       if (p.ll) {
@@ -1457,7 +1468,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
       if (A) mbar_wait_cluster(red_empty, 0u, no_abort);  // every peer's "drained" arrival
       else if (ntile > 1) mbar_wait_cluster(red_empty, (uint32_t)((ntile - 2) & 1), no_abort);
       *no_abort = 0;
-      if (FUSED && !p.ll && crank == 0)
+      if (FUSED && !p.ll && !solo && crank == 0)
         mbar_wait_cluster(pub_bar, (uint32_t)((ntile - 1) & 1), no_abort);
       if (FUSED && p.norm) {  // the leader's rstd here, and (leader) every CTA's row sums
         *no_abort = 0;
@@ -2108,9 +2119,11 @@ int fused_args(b2_nvar* h, const void* a, const void* qw, const void* qz, const 
   args.ll = (view->slot_bytes >= (unsigned long long)M * N * 8 && tuning(B2_TUNE_AR_FLAGS) == 0)
                 ? 1 : 0;
   // Two-shot moves 2 (P-1)/P of the payload per rank over NVLink instead of P-1 times it, for one
-  // more hop of latency: the choice from 4 ranks up (B2_TUNE_AR_TWO_SHOT: 1 on, 2 off).
+  // more hop of latency. Measured at 4 ranks on NVLink, one-shot is faster (config 4 step 3,298 µs
+  // against 3,448; down_proj shard 16.5 against 17.9 µs), so two-shot is the choice from 8 ranks
+  // up, where one-shot would move 7x the payload per rank (B2_TUNE_AR_TWO_SHOT: 1 on, 2 off).
   const int ts = tuning(B2_TUNE_AR_TWO_SHOT);
-  args.two_shot = args.ll && (ts == 1 || (ts == 0 && view->world >= 4)) ? 1 : 0;
+  args.two_shot = args.ll && (ts == 1 || (ts == 0 && view->world >= 8)) ? 1 : 0;
   if (norm) {
     args.norm = 1;
     args.eps = eps;
