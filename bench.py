@@ -277,30 +277,47 @@ class DecodeModel:
         # attention and the activation are not part of this path)
         self.a_o = (torch.randn(M, c["o_in"] // P, device="cuda", generator=g) * 0.05).half()
         self.a_d = (torch.randn(M, c["inter"] // P, device="cuda", generator=g) * 0.05).half()
-        self.norm, self.h1 = norm, h1
+        self.norm, self.h1, self.packed = norm, h1, False
         self.res = torch.empty(M, H, device="cuda", dtype=torch.float16)
         self.nw = [(1.0 + (torch.rand(2, H, device="cuda", generator=g) - 0.5) * 0.2).half()
                    for _ in range(c["layers"])]
 
-    def row_parallel(self, a, w):
-        return self.ar.w4_gemm_all_reduce(a, *w) if self.ar else self.ops.w4gemm(a, *w, 0, 0)
+    def pack(self):
+        """Repack the weights at load time (w4_repack) for every launch that runs the plain W4
+        GEMM: qkv and gate_up, and o and down at TP=1 (the fused all-reduce kernels read the GPTQ
+        layout). `packed` then switches those launches to w4gemm_packed."""
+        kinds = ("qkv", "gate_up") + (("o", "down") if self.ar is None else ())
+        for L in self.layers:
+            for k in kinds:
+                L["packed_" + k] = self.ops.w4_repack(*L[k])
+        self.packed = True
 
-    def row_parallel_norm(self, a, w, nw):
+    def w4(self, a, L, kind):
+        pk = L.get("packed_" + kind) if self.packed else None
+        if pk is not None:
+            return self.ops.w4gemm_packed(a, pk, L[kind][0].shape[1], CFG4["G"])
+        return self.ops.w4gemm(a, *L[kind], 0, 0)
+
+    def row_parallel(self, a, L, kind):
+        return self.ar.w4_gemm_all_reduce(a, *L[kind]) if self.ar else self.w4(a, L, kind)
+
+    def row_parallel_norm(self, a, L, kind, nw):
         """Row-parallel GEMM, all-reduce, then residual add + RMSNorm (fused or not)."""
         eps = 1e-6
+        w = L[kind]
         if self.norm == "fused":
             if self.ar:
                 return self.ar.w4_gemm_all_reduce_rmsnorm(a, *w, self.res, nw, eps)
             return self.ops.w4gemm_ar_rmsnorm(a, *w, self.h1, self.res, nw, eps)
-        y = self.row_parallel(a, w)
+        y = self.row_parallel(a, L, kind)
         xf = y.float() + self.res.float()
         self.res.copy_(xf.half())
         return ((xf * (xf.pow(2).mean(dim=-1, keepdim=True) + eps).rsqrt()).half() * nw)
 
     def launch(self, kind: str, L: dict, h):
         if kind in ("o", "down"):
-            return self.row_parallel(self.a_o if kind == "o" else self.a_d, L[kind])
-        return self.ops.w4gemm(h, *L[kind], 0, 0)
+            return self.row_parallel(self.a_o if kind == "o" else self.a_d, L, kind)
+        return self.w4(h, L, kind)
 
     def step(self):
         h = self.x0
@@ -308,9 +325,9 @@ class DecodeModel:
             self.res.copy_(self.x0)
             for L, nw in zip(self.layers, self.nw):
                 self.launch("qkv", L, h)
-                h = self.row_parallel_norm(self.a_o, L["o"], nw[0])
+                h = self.row_parallel_norm(self.a_o, L, "o", nw[0])
                 self.launch("gate_up", L, h)
-                h = self.row_parallel_norm(self.a_d, L["down"], nw[1])
+                h = self.row_parallel_norm(self.a_d, L, "down", nw[1])
             return self.ops.gemm(h, self.lm, 0)
         for L in self.layers:
             self.launch("qkv", L, h)
@@ -526,6 +543,22 @@ def run_gpu(args):
     norms["norms_per_step"] = 2 * c["layers"]
 
     kernels = kernel_breakdown(model, world, capi)
+
+    # the same step with the weights repacked at load time (w4_repack, then w4gemm_packed for the
+    # launches without a fused all-reduce); the logits must be bit-identical
+    ref = model.step()
+    model.pack()
+    eager_p = model.step()
+    torch.cuda.synchronize()
+    g_p, out_p = capture(model.step)
+    for _ in range(args.warmup):
+        g_p.replay()
+    torch.cuda.synchronize()
+    ms = time_steps(g_p.replay, args.steps, world, stream)
+    packed = {"us_per_step": round(max_over_ranks(ms * 1e3 / args.steps, world), 1),
+              "repacked": ["qkv", "gate_up"] + (["o", "down"] if P == 1 else []),
+              "logits_equal_plain": bool(torch.equal(ref, eager_p) and torch.equal(out_p, eager_p))}
+    del g_p
     status = ar.status() if ar else ops.workspace_status(False)
     peak, peak_kind = hbm_peak()
     nbytes = decode_step_bytes(P)
@@ -569,6 +602,7 @@ def run_gpu(args):
                          "traffic": recorded_traffic(dom["kernel"].split("<")[0], workload)},
             "kernels": kernels,
             "config4_with_norms": norms,
+            "config4_packed_weights": packed,
             "gpu_launches": args.steps * (4 * c["layers"] + 1),
             "graph_equals_eager": same, "device_status": int(status),
             "clocks": clk.summary(),

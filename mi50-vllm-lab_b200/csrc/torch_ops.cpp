@@ -6,9 +6,9 @@
 //   w4gemm(Tensor a, Tensor qw, Tensor qz, Tensor sc, int kw, int waves) kernels/w4.cu:506-509
 //   hostar_create / hostar_unlink / hostar_max_bytes / hostar_allreduce kernels/hostar.cu:155-166
 // plus operators the reference does not have (N-rank NVLink all-reduce, the W4 GEMM with the
-// all-reduce fused into its epilogue, optionally followed by the residual add + RMSNorm, status
-// and tuning). Device operators are registered on the
-// CUDA dispatch key and launch on the current stream; host operators on
+// all-reduce fused into its epilogue, optionally followed by the residual add + RMSNorm, the
+// load-time weight repack and the W4 GEMM on its image, status and tuning). Device operators
+// are registered on the CUDA dispatch key and launch on the current stream; host operators on
 // CompositeExplicitAutograd, as in the reference. Errors become RuntimeError via TORCH_CHECK.
 //
 // The tuning selectors of the reference (`variant` of gemm, `kw`/`waves` of w4gemm) are accepted
@@ -139,6 +139,73 @@ at::Tensor w4_gemm_meta(const at::Tensor& a, const at::Tensor& qw, const at::Ten
                         const at::Tensor& sc, int64_t kw, int64_t waves) {
   (void)qz, (void)sc, (void)kw, (void)waves;
   return at::empty({a.size(0), qw.size(1)}, a.options());
+}
+
+// ------------------------------------------------------------------------------------------------
+// Load-time repack (no counterpart in the reference). w4_repack(qw, qz, sc) returns the packed
+// uint8 image of b2_w4_repack; w4gemm_packed(a, packed, N, group_size) is w4gemm on that image.
+// The image is opaque, so N and the group size travel with the call; K is a.size(1).
+// ------------------------------------------------------------------------------------------------
+at::Tensor w4_repack(const at::Tensor& qw, const at::Tensor& qz, const at::Tensor& sc) {
+  check_cuda_half(sc, "w4_repack", "sc");
+  TORCH_CHECK(qw.is_cuda() && qz.is_cuda(), "w4_repack: qw and qz must be CUDA tensors");
+  TORCH_CHECK(qw.scalar_type() == at::kInt && qz.scalar_type() == at::kInt,
+              "w4_repack: qw and qz must be int32");
+  TORCH_CHECK(qw.is_contiguous() && qz.is_contiguous(), "w4_repack: qw and qz must be contiguous");
+  TORCH_CHECK(qw.dim() == 2 && qz.dim() == 2 && sc.dim() == 2, "w4_repack: operands must be 2-D");
+  const int64_t K = qw.size(0) * 8, N = qw.size(1);
+  TORCH_CHECK(sc.size(0) > 0 && K % sc.size(0) == 0 && sc.size(1) == N,
+              "w4_repack: sc must be [K/G, N]; got ", sc.sizes());
+  TORCH_CHECK(qz.size(0) == sc.size(0) && qz.size(1) * 8 == N,
+              "w4_repack: qz must be [K/G, N/8]; got ", qz.sizes());
+  const int G = (int)(K / sc.size(0));
+  const size_t bytes = b2_w4_packed_bytes((int)K, (int)N, G);
+  TORCH_CHECK(bytes > 0, "w4_repack: K=", K, " N=", N, " G=", G, " outside the W4 contract");
+  c10::cuda::CUDAGuard guard(qw.device());
+  auto out = at::empty({(int64_t)bytes}, qw.options().dtype(at::kByte));
+  const int rc = b2_w4_repack(qw.data_ptr(), qz.data_ptr(), sc.data_ptr(), (int)K, (int)N, G,
+                              out.data_ptr(), bytes,
+                              c10::cuda::getCurrentCUDAStream(qw.get_device()).stream());
+  TORCH_CHECK(rc == B2_OK, "gfx906_skinny.w4_repack: ", detail(rc));
+  return out;
+}
+
+at::Tensor w4_gemm_packed(const at::Tensor& a, const at::Tensor& packed, int64_t N,
+                          int64_t group_size) {
+  check_cuda_half(a, "w4gemm_packed", "a");
+  TORCH_CHECK(packed.is_cuda() && packed.scalar_type() == at::kByte && packed.is_contiguous() &&
+                  packed.dim() == 1,
+              "w4gemm_packed: packed must be the contiguous uint8 tensor w4_repack returns");
+  TORCH_CHECK(a.dim() == 2, "w4gemm_packed: a must be 2-D");
+  const int64_t M = a.size(0), K = a.size(1);
+  TORCH_CHECK(M >= 1 && M <= 8, "w4gemm_packed: M=", M, " outside 1..8");
+  const size_t bytes = b2_w4_packed_bytes((int)K, (int)N, (int)group_size);
+  TORCH_CHECK(bytes > 0 && (size_t)packed.numel() >= bytes, "w4gemm_packed: packed holds ",
+              packed.numel(), " bytes; K=", K, " N=", N, " G=", group_size, " needs ", bytes);
+  c10::cuda::CUDAGuard guard(a.device());
+  auto y = at::empty({M, N}, a.options());
+  const int dev = a.get_device();
+  void* ws = workspace(dev);
+  const int rc = b2_w4_gemm_packed(a.data_ptr(), packed.data_ptr(), y.data_ptr(), (int)M, (int)K,
+                                   (int)N, (int)group_size, ws, b2_workspace_bytes(dev),
+                                   c10::cuda::getCurrentCUDAStream(dev).stream());
+  TORCH_CHECK(rc == B2_OK, "gfx906_skinny.w4gemm_packed: ", detail(rc));
+  return y;
+}
+
+at::Tensor w4_repack_meta(const at::Tensor& qw, const at::Tensor& qz, const at::Tensor& sc) {
+  (void)qz;
+  const int64_t K = qw.size(0) * 8, N = qw.size(1);
+  TORCH_CHECK(sc.size(0) > 0 && K % sc.size(0) == 0, "w4_repack: sc must be [K/G, N]");
+  const size_t bytes = b2_w4_packed_bytes((int)K, (int)N, (int)(K / sc.size(0)));
+  TORCH_CHECK(bytes > 0, "w4_repack: K=", K, " N=", N, " outside the W4 contract");
+  return at::empty({(int64_t)bytes}, qw.options().dtype(at::kByte));
+}
+
+at::Tensor w4_gemm_packed_meta(const at::Tensor& a, const at::Tensor& packed, int64_t N,
+                               int64_t group_size) {
+  (void)packed, (void)group_size;
+  return at::empty({a.size(0), N}, a.options());
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -339,6 +406,8 @@ TORCH_LIBRARY(gfx906_skinny, m) {
   m.def("w4gemm_ar(Tensor a, Tensor qw, Tensor qz, Tensor sc, int handle) -> Tensor");
   m.def("w4gemm_ar_rmsnorm(Tensor a, Tensor qw, Tensor qz, Tensor sc, int handle, "
         "Tensor(a!) residual, Tensor weight, float eps) -> Tensor");
+  m.def("w4_repack(Tensor qw, Tensor qz, Tensor sc) -> Tensor");
+  m.def("w4gemm_packed(Tensor a, Tensor packed, int N, int group_size) -> Tensor");
   m.def("nvar_status(int handle, bool clear=False) -> int");
   m.def("nvar_set_timeout_ms(int handle, int ms) -> ()");
   m.def("workspace_status(bool clear=False) -> int");
@@ -348,6 +417,8 @@ TORCH_LIBRARY(gfx906_skinny, m) {
 TORCH_LIBRARY_IMPL(gfx906_skinny, CUDA, m) {
   m.impl("gemm", &skinny_gemm);
   m.impl("w4gemm", &w4_gemm);
+  m.impl("w4_repack", &w4_repack);
+  m.impl("w4gemm_packed", &w4_gemm_packed);
   m.impl("hostar_allreduce", &hostar_allreduce);
   m.impl("nvar_allreduce", &nvar_allreduce);
   m.impl("w4gemm_ar", &w4gemm_ar);
@@ -357,6 +428,8 @@ TORCH_LIBRARY_IMPL(gfx906_skinny, CUDA, m) {
 TORCH_LIBRARY_IMPL(gfx906_skinny, Meta, m) {
   m.impl("gemm", &skinny_gemm_meta);
   m.impl("w4gemm", &w4_gemm_meta);
+  m.impl("w4_repack", &w4_repack_meta);
+  m.impl("w4gemm_packed", &w4_gemm_packed_meta);
 }
 
 TORCH_LIBRARY_IMPL(gfx906_skinny, CompositeExplicitAutograd, m) {

@@ -53,6 +53,16 @@ def test_meta_shapes(ops):
     qz = torch.empty(4, 32, dtype=torch.int32, device="meta")
     sc = torch.empty(4, 256, dtype=torch.float16, device="meta")
     assert ops.w4gemm(x, qw, qz, sc, 128, 14).shape == (7, 256)
+    pk = ops.w4_repack(qw, qz, sc)
+    assert pk.dtype == torch.uint8 and pk.numel() >= 512 * 256 // 2
+    assert ops.w4gemm_packed(x, pk, 256, 128).shape == (7, 256)
+
+
+def test_repack_operator_schemas(ops):
+    assert str(ops.w4_repack.default._schema) == \
+        "gfx906_skinny::w4_repack(Tensor qw, Tensor qz, Tensor sc) -> Tensor"
+    assert str(ops.w4gemm_packed.default._schema) == \
+        "gfx906_skinny::w4gemm_packed(Tensor a, Tensor packed, int N, int group_size) -> Tensor"
 
 
 _ALIGNED = 1 << 20  # a fake, 16-byte aligned address: validation fails before it is used

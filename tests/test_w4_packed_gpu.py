@@ -139,3 +139,30 @@ def test_packed_rejects(capi):
     assert lib.b2_w4_repack(p, p, p, K, N, G, p, need - 16, stream_ptr()) != 0   # too small
     assert lib.b2_w4_repack(p, p, p, K, N, G, p + 8, need, stream_ptr()) != 0    # misaligned
     assert lib.b2_w4_gemm_packed(p, 0, p, 1, K, N, G, p, t.numel(), stream_ptr()) != 0  # null
+
+
+@pytest.mark.parametrize("M,K,N,G", [(8, 1024, 384, 128), (3, 256, 96, 32), (7, 4096, 4096, 128)])
+def test_torch_ops_packed(ops, capi, oracle, M, K, N, G):
+    """torch.ops.gfx906_skinny.w4_repack / w4gemm_packed: the same bytes as the C ABI and the same
+    product as w4gemm, bit for bit."""
+    x, qw, qz, sc = (dev(a) for a in oracle.gen_w4(M, K, N, G, seed=M * K + N))
+    pk = ops.w4_repack(qw, qz, sc)
+    assert pk.dtype == torch.uint8 and pk.numel() == capi.lib().b2_w4_packed_bytes(K, N, G)
+    assert torch.equal(pk, repack(capi, qw, qz, sc, K, N, G))
+    y = ops.w4gemm(x, qw, qz, sc, 0, 0)
+    yp = ops.w4gemm_packed(x, pk, N, G)
+    torch.cuda.synchronize()
+    assert torch.equal(y, yp), mismatch(yp, y)
+
+
+def test_torch_ops_packed_rejects(ops, oracle):
+    x, qw, qz, sc = (dev(a) for a in oracle.gen_w4(2, 256, 64, 128, seed=5))
+    pk = ops.w4_repack(qw, qz, sc)
+    with pytest.raises(RuntimeError, match="needs"):
+        ops.w4gemm_packed(x, pk[:-16], 64, 128)          # image shorter than K, N, G need
+    with pytest.raises(RuntimeError, match="G=96 needs 0"):
+        ops.w4gemm_packed(x, pk, 64, 96)                 # group size outside the contract
+    with pytest.raises(RuntimeError, match="uint8"):
+        ops.w4gemm_packed(x, pk.view(torch.int32), 64, 128)
+    with pytest.raises(RuntimeError, match="qz must be"):
+        ops.w4_repack(qw, qz[:, :4], sc)
