@@ -283,29 +283,39 @@ class DecodeModel:
                    for _ in range(c["layers"])]
 
     def pack(self):
-        """Repack the weights at load time (w4_repack) for every launch that runs the plain W4
-        GEMM: qkv and gate_up, and o and down at TP=1 (the fused all-reduce kernels read the GPTQ
-        layout). `packed` then switches those launches to w4gemm_packed."""
-        kinds = ("qkv", "gate_up") + (("o", "down") if self.ar is None else ())
+        """Repack every layer's weights at load time (w4_repack); `packed` then switches the
+        launches to the operators on the packed image (w4gemm_packed, w4gemm_ar_packed,
+        w4gemm_ar_rmsnorm_packed)."""
         for L in self.layers:
-            for k in kinds:
+            for k in ("qkv", "o", "gate_up", "down"):
                 L["packed_" + k] = self.ops.w4_repack(*L[k])
         self.packed = True
 
     def w4(self, a, L, kind):
-        pk = L.get("packed_" + kind) if self.packed else None
-        if pk is not None:
-            return self.ops.w4gemm_packed(a, pk, L[kind][0].shape[1], CFG4["G"])
+        if self.packed:
+            return self.ops.w4gemm_packed(a, L["packed_" + kind], L[kind][0].shape[1], CFG4["G"])
         return self.ops.w4gemm(a, *L[kind], 0, 0)
 
     def row_parallel(self, a, L, kind):
-        return self.ar.w4_gemm_all_reduce(a, *L[kind]) if self.ar else self.w4(a, L, kind)
+        if not self.ar:
+            return self.w4(a, L, kind)
+        if self.packed:
+            return self.ar.w4_gemm_all_reduce_packed(a, L["packed_" + kind], L[kind][0].shape[1],
+                                                     CFG4["G"])
+        return self.ar.w4_gemm_all_reduce(a, *L[kind])
 
     def row_parallel_norm(self, a, L, kind, nw):
         """Row-parallel GEMM, all-reduce, then residual add + RMSNorm (fused or not)."""
         eps = 1e-6
         w = L[kind]
         if self.norm == "fused":
+            if self.packed:
+                n, pk = w[0].shape[1], L["packed_" + kind]
+                if self.ar:
+                    return self.ar.w4_gemm_all_reduce_rmsnorm_packed(a, pk, n, CFG4["G"], self.res,
+                                                                     nw, eps)
+                return self.ops.w4gemm_ar_rmsnorm_packed(a, pk, n, CFG4["G"], self.h1, self.res,
+                                                         nw, eps)
             if self.ar:
                 return self.ar.w4_gemm_all_reduce_rmsnorm(a, *w, self.res, nw, eps)
             return self.ops.w4gemm_ar_rmsnorm(a, *w, self.h1, self.res, nw, eps)
@@ -556,7 +566,8 @@ def run_gpu(args):
     torch.cuda.synchronize()
     ms = time_steps(g_p.replay, args.steps, world, stream)
     packed = {"us_per_step": round(max_over_ranks(ms * 1e3 / args.steps, world), 1),
-              "repacked": ["qkv", "gate_up"] + (["o", "down"] if P == 1 else []),
+              "operators": "w4_repack once per weight; w4gemm_packed"
+                           + (", w4gemm_ar_packed" if P > 1 else "") + ", gemm",
               "logits_equal_plain": bool(torch.equal(ref, eager_p) and torch.equal(out_p, eager_p))}
     del g_p
     status = ar.status() if ar else ops.workspace_status(False)

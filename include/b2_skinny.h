@@ -242,6 +242,15 @@ int b2_w4_gemm_allreduce_rmsnorm(b2_nvar* ar, const void* a, const void* qw, con
                                  const void* sc, void* residual, const void* norm_weight,
                                  float eps, void* y, int M, int K, int N, int group_size,
                                  void* ws, size_t ws_bytes, void* stream);
+/* The two fused layers on weights repacked by b2_w4_repack (`packed` in place of qw, qz, sc);
+ * the same contract and the same bits as the calls above on the original tensors. */
+int b2_w4_gemm_allreduce_packed(b2_nvar* ar, const void* a, const void* packed, void* y, int M,
+                                int K, int N, int group_size, void* ws, size_t ws_bytes,
+                                void* stream);
+int b2_w4_gemm_allreduce_rmsnorm_packed(b2_nvar* ar, const void* a, const void* packed,
+                                        void* residual, const void* norm_weight, float eps,
+                                        void* y, int M, int K, int N, int group_size, void* ws,
+                                        size_t ws_bytes, void* stream);
 /* Synchronously read the device error word of the handle (0 or B2_ERR_TIMEOUT). Clearing a
  * timeout also resets the grid-wide barrier count of b2_w4_gemm_allreduce_rmsnorm, which a
  * launch that gave up may have left behind: clear it before the next call. */

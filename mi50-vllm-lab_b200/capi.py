@@ -64,6 +64,9 @@ _SIGS = {
     "b2_w4_gemm_allreduce": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
     "b2_w4_gemm_allreduce_rmsnorm": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, C.c_float, _vp, _i, _i,
                                           _i, _i, _vp, _sz, _vp]),
+    "b2_w4_gemm_allreduce_packed": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _sz, _vp]),
+    "b2_w4_gemm_allreduce_rmsnorm_packed": (_i, [_vp, _vp, _vp, _vp, _vp, C.c_float, _vp, _i, _i,
+                                                 _i, _i, _vp, _sz, _vp]),
     "b2_nvar_status": (_i, [_vp, _i, C.POINTER(_i)]),
     "b2_nvar_rank": (_i, [_vp]),
     "b2_nvar_world": (_i, [_vp]),

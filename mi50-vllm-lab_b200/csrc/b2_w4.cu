@@ -2153,6 +2153,20 @@ int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* q
   return dispatch<true>(args, qw, qz, sc, &v, stream, /*early=*/true);
 }
 
+// The fused launch on weights repacked by w4_repack (`packed` in place of qw, qz, sc).
+int launch_w4_allreduce_packed(b2_nvar* h, const void* a, const void* packed, void* y, int M,
+                               int K, int N, int G, void* ws, size_t ws_bytes,
+                               cudaStream_t stream, void* residual, const void* nw, float eps) {
+  W4Args args;
+  ArView v;
+  const int rc = fused_args(h, a, packed, packed, packed, y, M, K, N, G, ws, ws_bytes, residual,
+                            nw, eps, &args, &v);
+  if (rc) return rc;
+  args.pk = static_cast<const uint8_t*>(packed);
+  args.pk_unit = packed_unit_bytes(G);
+  return dispatch<true>(args, nullptr, nullptr, nullptr, &v, stream, /*early=*/true);
+}
+
 // `R` ranks of one group in one cooperative launch on this GPU (grid.y = rank). Every rank gets
 // 1/R of the GPU in the plan, and the cooperative attribute makes the launch fail rather than
 // start with CTAs that cannot all be resident.
@@ -2274,6 +2288,27 @@ extern "C" int b2_w4_gemm_allreduce_rmsnorm(b2_nvar* ar, const void* a, const vo
     return b2::fail(B2_ERR_INVALID_ARG, "w4_allreduce_rmsnorm: null residual or norm_weight");
   return b2::launch_w4_allreduce(ar, a, qw, qz, sc, y, M, K, N, group_size, ws, ws_bytes,
                                  static_cast<cudaStream_t>(stream), residual, norm_weight, eps);
+}
+
+extern "C" int b2_w4_gemm_allreduce_packed(b2_nvar* ar, const void* a, const void* packed,
+                                           void* y, int M, int K, int N, int group_size,
+                                           void* ws, size_t ws_bytes, void* stream) {
+  if (!ar) return b2::fail(B2_ERR_STATE, "w4_allreduce: null all-reduce handle");
+  return b2::launch_w4_allreduce_packed(ar, a, packed, y, M, K, N, group_size, ws, ws_bytes,
+                                        static_cast<cudaStream_t>(stream), nullptr, nullptr, 0.f);
+}
+
+extern "C" int b2_w4_gemm_allreduce_rmsnorm_packed(b2_nvar* ar, const void* a, const void* packed,
+                                                   void* residual, const void* norm_weight,
+                                                   float eps, void* y, int M, int K, int N,
+                                                   int group_size, void* ws, size_t ws_bytes,
+                                                   void* stream) {
+  if (!ar) return b2::fail(B2_ERR_STATE, "w4_allreduce_rmsnorm: null all-reduce handle");
+  if (!residual || !norm_weight)
+    return b2::fail(B2_ERR_INVALID_ARG, "w4_allreduce_rmsnorm: null residual or norm_weight");
+  return b2::launch_w4_allreduce_packed(ar, a, packed, y, M, K, N, group_size, ws, ws_bytes,
+                                        static_cast<cudaStream_t>(stream), residual, norm_weight,
+                                        eps);
 }
 
 // Ranks of one group emulated on one GPU in one cooperative launch; see include/b2_skinny.h.

@@ -170,18 +170,25 @@ at::Tensor w4_repack(const at::Tensor& qw, const at::Tensor& qz, const at::Tenso
   return out;
 }
 
-at::Tensor w4_gemm_packed(const at::Tensor& a, const at::Tensor& packed, int64_t N,
-                          int64_t group_size) {
-  check_cuda_half(a, "w4gemm_packed", "a");
+void check_packed(const at::Tensor& a, const at::Tensor& packed, int64_t N, int64_t group_size,
+                  const char* op) {
+  check_cuda_half(a, op, "a");
   TORCH_CHECK(packed.is_cuda() && packed.scalar_type() == at::kByte && packed.is_contiguous() &&
                   packed.dim() == 1,
-              "w4gemm_packed: packed must be the contiguous uint8 tensor w4_repack returns");
-  TORCH_CHECK(a.dim() == 2, "w4gemm_packed: a must be 2-D");
+              op, ": packed must be the contiguous uint8 tensor w4_repack returns");
+  TORCH_CHECK(packed.device() == a.device(), op, ": a and packed on different devices");
+  TORCH_CHECK(a.dim() == 2, op, ": a must be 2-D");
   const int64_t M = a.size(0), K = a.size(1);
-  TORCH_CHECK(M >= 1 && M <= 8, "w4gemm_packed: M=", M, " outside 1..8");
+  TORCH_CHECK(M >= 1 && M <= 8, op, ": M=", M, " outside 1..8");
   const size_t bytes = b2_w4_packed_bytes((int)K, (int)N, (int)group_size);
-  TORCH_CHECK(bytes > 0 && (size_t)packed.numel() >= bytes, "w4gemm_packed: packed holds ",
+  TORCH_CHECK(bytes > 0 && (size_t)packed.numel() >= bytes, op, ": packed holds ",
               packed.numel(), " bytes; K=", K, " N=", N, " G=", group_size, " needs ", bytes);
+}
+
+at::Tensor w4_gemm_packed(const at::Tensor& a, const at::Tensor& packed, int64_t N,
+                          int64_t group_size) {
+  check_packed(a, packed, N, group_size, "w4gemm_packed");
+  const int64_t M = a.size(0), K = a.size(1);
   c10::cuda::CUDAGuard guard(a.device());
   auto y = at::empty({M, N}, a.options());
   const int dev = a.get_device();
@@ -353,6 +360,51 @@ at::Tensor w4gemm_ar_rmsnorm(const at::Tensor& a, const at::Tensor& qw, const at
   return y;
 }
 
+// w4gemm_ar and w4gemm_ar_rmsnorm on weights repacked by w4_repack
+at::Tensor w4gemm_ar_packed(const at::Tensor& a, const at::Tensor& packed, int64_t N,
+                            int64_t group_size, int64_t handle) {
+  check_packed(a, packed, N, group_size, "w4gemm_ar_packed");
+  ArEntry& e = connected_entry(handle, "w4gemm_ar_packed");
+  const int64_t M = a.size(0), K = a.size(1);
+  c10::cuda::CUDAGuard guard(a.device());
+  auto y = at::empty({M, N}, a.options());
+  const int dev = a.get_device();
+  void* ws = workspace(dev);
+  const int rc = b2_w4_gemm_allreduce_packed(e.ar, a.data_ptr(), packed.data_ptr(), y.data_ptr(),
+                                             (int)M, (int)K, (int)N, (int)group_size, ws,
+                                             b2_workspace_bytes(dev),
+                                             c10::cuda::getCurrentCUDAStream(dev).stream());
+  TORCH_CHECK(rc == B2_OK, "gfx906_skinny.w4gemm_ar_packed: ", detail(rc));
+  return y;
+}
+
+at::Tensor w4gemm_ar_rmsnorm_packed(const at::Tensor& a, const at::Tensor& packed, int64_t N,
+                                    int64_t group_size, int64_t handle, at::Tensor& residual,
+                                    const at::Tensor& weight, double eps) {
+  const char* op = "w4gemm_ar_rmsnorm_packed";
+  check_packed(a, packed, N, group_size, op);
+  check_cuda_half(residual, op, "residual");
+  check_cuda_half(weight, op, "weight");
+  const int64_t M = a.size(0), K = a.size(1);
+  TORCH_CHECK(residual.dim() == 2 && residual.size(0) == M && residual.size(1) == N, op,
+              ": residual must be [M, N]; got ", residual.sizes());
+  TORCH_CHECK(weight.dim() == 1 && weight.size(0) == N, op, ": weight must be [N]; got ",
+              weight.sizes());
+  TORCH_CHECK(residual.device() == a.device() && weight.device() == a.device(), op,
+              ": residual and weight must be on the input's device");
+  ArEntry& e = connected_entry(handle, op);
+  c10::cuda::CUDAGuard guard(a.device());
+  auto y = at::empty({M, N}, a.options());
+  const int dev = a.get_device();
+  void* ws = workspace(dev);
+  const int rc = b2_w4_gemm_allreduce_rmsnorm_packed(
+      e.ar, a.data_ptr(), packed.data_ptr(), residual.data_ptr(), weight.data_ptr(), (float)eps,
+      y.data_ptr(), (int)M, (int)K, (int)N, (int)group_size, ws, b2_workspace_bytes(dev),
+      c10::cuda::getCurrentCUDAStream(dev).stream());
+  TORCH_CHECK(rc == B2_OK, "gfx906_skinny.w4gemm_ar_rmsnorm_packed: ", detail(rc));
+  return y;
+}
+
 int64_t nvar_status(int64_t handle, bool clear) {
   ArEntry* e;
   {
@@ -408,6 +460,9 @@ TORCH_LIBRARY(gfx906_skinny, m) {
         "Tensor(a!) residual, Tensor weight, float eps) -> Tensor");
   m.def("w4_repack(Tensor qw, Tensor qz, Tensor sc) -> Tensor");
   m.def("w4gemm_packed(Tensor a, Tensor packed, int N, int group_size) -> Tensor");
+  m.def("w4gemm_ar_packed(Tensor a, Tensor packed, int N, int group_size, int handle) -> Tensor");
+  m.def("w4gemm_ar_rmsnorm_packed(Tensor a, Tensor packed, int N, int group_size, int handle, "
+        "Tensor(a!) residual, Tensor weight, float eps) -> Tensor");
   m.def("nvar_status(int handle, bool clear=False) -> int");
   m.def("nvar_set_timeout_ms(int handle, int ms) -> ()");
   m.def("workspace_status(bool clear=False) -> int");
@@ -423,6 +478,8 @@ TORCH_LIBRARY_IMPL(gfx906_skinny, CUDA, m) {
   m.impl("nvar_allreduce", &nvar_allreduce);
   m.impl("w4gemm_ar", &w4gemm_ar);
   m.impl("w4gemm_ar_rmsnorm", &w4gemm_ar_rmsnorm);
+  m.impl("w4gemm_ar_packed", &w4gemm_ar_packed);
+  m.impl("w4gemm_ar_rmsnorm_packed", &w4gemm_ar_rmsnorm_packed);
 }
 
 TORCH_LIBRARY_IMPL(gfx906_skinny, Meta, m) {

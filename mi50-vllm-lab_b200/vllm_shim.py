@@ -136,6 +136,15 @@ class NvlinkAllReduce:
         rows are returned."""
         return self.ops.w4gemm_ar_rmsnorm(x, w_q, w_zp, w_s, self.handle, residual, weight, eps)
 
+    def w4_gemm_all_reduce_packed(self, x, packed, n: int, group_size: int) -> torch.Tensor:
+        """w4_gemm_all_reduce on weights repacked at load time (w4_repack); n = output width."""
+        return self.ops.w4gemm_ar_packed(x, packed, n, group_size, self.handle)
+
+    def w4_gemm_all_reduce_rmsnorm_packed(self, x, packed, n: int, group_size: int, residual,
+                                          weight, eps: float) -> torch.Tensor:
+        return self.ops.w4gemm_ar_rmsnorm_packed(x, packed, n, group_size, self.handle, residual,
+                                                 weight, eps)
+
     def status(self, clear: bool = False) -> int:
         return int(self.ops.nvar_status(self.handle, clear))
 

@@ -221,6 +221,18 @@ def main():
     if ar.status() != 0:
         fail(f"fused RMSNorm status {ar.status()}")
 
+    # 3d. both fused layers on this rank's shard repacked at load time (w4_repack): the same bits
+    pks = ar.ops.w4_repack(qws, qzs, scs)
+    yp = ar.w4_gemm_all_reduce_packed(xs, pks, N, G)
+    rp = res0.clone()
+    ynp = ar.w4_gemm_all_reduce_rmsnorm_packed(xs, pks, N, G, rp, wn, 1e-6)
+    torch.cuda.synchronize()
+    if not (torch.equal(yp, yf) and torch.equal(ynp, yn) and torch.equal(rp, rn)):
+        fail("fused layers on repacked weights differ from the same layers on GPTQ tensors")
+    if ar.status() != 0:
+        fail(f"fused packed status {ar.status()}")
+    del pks
+
     # 3b. the same layer through the other split-K kernel's fused epilogue (the default is the
     # cluster kernel; B2_TUNE_W4_PATH = 1 selects stream-K with its global fix-up)
     from mi50_vllm_lab_b200 import capi

@@ -63,6 +63,12 @@ def test_repack_operator_schemas(ops):
         "gfx906_skinny::w4_repack(Tensor qw, Tensor qz, Tensor sc) -> Tensor"
     assert str(ops.w4gemm_packed.default._schema) == \
         "gfx906_skinny::w4gemm_packed(Tensor a, Tensor packed, int N, int group_size) -> Tensor"
+    assert str(ops.w4gemm_ar_packed.default._schema) == \
+        "gfx906_skinny::w4gemm_ar_packed(Tensor a, Tensor packed, int N, int group_size, " \
+        "int handle) -> Tensor"
+    assert str(ops.w4gemm_ar_rmsnorm_packed.default._schema) == \
+        "gfx906_skinny::w4gemm_ar_rmsnorm_packed(Tensor a, Tensor packed, int N, int group_size, " \
+        "int handle, Tensor(a!) residual, Tensor weight, float eps) -> Tensor"
 
 
 _ALIGNED = 1 << 20  # a fake, 16-byte aligned address: validation fails before it is used

@@ -7,6 +7,9 @@ plan, same bytes in shared memory); both are also checked against the float64 re
 
 from __future__ import annotations
 
+import ctypes
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -166,3 +169,88 @@ def test_torch_ops_packed_rejects(ops, oracle):
         ops.w4gemm_packed(x, pk.view(torch.int32), 64, 128)
     with pytest.raises(RuntimeError, match="qz must be"):
         ops.w4_repack(qw, qz[:, :4], sc)
+
+
+FUSED = [(8, 1024, 384, 128), (5, 512, 256, 64), (3, 4096, 1024, 32), (8, 2176, 5120, 128)]
+
+
+@pytest.fixture(scope="module")
+def solo(capi):
+    """One-rank all-reduce handle on device 0: the fused kernels run their whole epilogue."""
+    lib = capi.lib()
+    h = ctypes.c_void_p()
+    capi.check(lib.b2_nvar_create(0, 0, 1, 8 * 8192 * 4, ctypes.byref(h)), "nvar_create")
+    yield h
+    torch.cuda.synchronize()
+    capi.check(lib.b2_nvar_destroy(h), "nvar_destroy")
+
+
+@pytest.mark.parametrize("path", [1, 2], ids=["stream-K", "cluster"])
+@pytest.mark.parametrize("M,K,N,G", FUSED)
+def test_fused_packed_equals_unpacked(capi, oracle, solo, path, M, K, N, G):
+    """b2_w4_gemm_allreduce(_rmsnorm)_packed give the bits of the same calls on the original
+    tensors: the output, and for the norm the normalised rows and the updated residual."""
+    lib = capi.lib()
+    saved = lib.b2_get_tuning(4)
+    lib.b2_set_tuning(4, path)
+    try:
+        ws = workspace(capi)
+        x, qw, qz, sc = oracle.gen_w4(M, K, N, G, seed=3 * M + K + N)
+        xd, qwd, qzd, scd = dev(x), dev(qw), dev(qz), dev(sc)
+        pk = repack(capi, qwd, qzd, scd, K, N, G)
+        sp = stream_ptr()
+        y0, y1 = (torch.empty(M, N, dtype=torch.float16, device="cuda") for _ in range(2))
+        capi.check(lib.b2_w4_gemm_allreduce(solo, xd.data_ptr(), qwd.data_ptr(), qzd.data_ptr(),
+                                            scd.data_ptr(), y0.data_ptr(), M, K, N, G,
+                                            ws.data_ptr(), ws.numel(), sp), "w4_gemm_allreduce")
+        capi.check(lib.b2_w4_gemm_allreduce_packed(solo, xd.data_ptr(), pk.data_ptr(),
+                                                   y1.data_ptr(), M, K, N, G, ws.data_ptr(),
+                                                   ws.numel(), sp), "w4_gemm_allreduce_packed")
+        rng = np.random.default_rng(M + N)
+        res = dev((rng.standard_normal((M, N)) * 4).astype(np.float16))
+        w = dev((1.0 + rng.uniform(-0.3, 0.3, size=N)).astype(np.float16))
+        r0, r1 = res.clone(), res.clone()
+        o0, o1 = (torch.empty(M, N, dtype=torch.float16, device="cuda") for _ in range(2))
+        capi.check(lib.b2_w4_gemm_allreduce_rmsnorm(
+            solo, xd.data_ptr(), qwd.data_ptr(), qzd.data_ptr(), scd.data_ptr(), r0.data_ptr(),
+            w.data_ptr(), 1e-6, o0.data_ptr(), M, K, N, G, ws.data_ptr(), ws.numel(), sp),
+            "w4_gemm_allreduce_rmsnorm")
+        capi.check(lib.b2_w4_gemm_allreduce_rmsnorm_packed(
+            solo, xd.data_ptr(), pk.data_ptr(), r1.data_ptr(), w.data_ptr(), 1e-6, o1.data_ptr(),
+            M, K, N, G, ws.data_ptr(), ws.numel(), sp), "w4_gemm_allreduce_rmsnorm_packed")
+        torch.cuda.synchronize()
+        assert torch.equal(y0, y1), mismatch(y1, y0)
+        assert torch.equal(o0, o1), mismatch(o1, o0)
+        assert torch.equal(r0, r1), mismatch(r1, r0)
+        check(y1, oracle.w4_ref(x, qw, qz, sc), f"fused packed path {path} M={M} K={K} N={N}")
+        st = ctypes.c_int()
+        capi.check(lib.b2_nvar_status(solo, 1, ctypes.byref(st)), "nvar_status")
+        assert st.value == 0
+    finally:
+        lib.b2_set_tuning(4, saved)
+
+
+def test_torch_ops_fused_packed(ops, oracle):
+    """w4gemm_ar_packed / w4gemm_ar_rmsnorm_packed on a one-rank handle from nvar_create equal
+    w4gemm_ar / w4gemm_ar_rmsnorm on the original tensors."""
+    M, K, N, G = 6, 2048, 3072, 128
+    x, qw, qz, sc = (dev(a) for a in oracle.gen_w4(M, K, N, G, seed=21))
+    name = f"/b2_test_packed_{os.getpid()}"
+    h = ops.nvar_create(name, M * N * 4, 0, 1)
+    ops.hostar_unlink(name)
+    pk = ops.w4_repack(qw, qz, sc)
+    assert torch.equal(ops.w4gemm_ar(x, qw, qz, sc, h), ops.w4gemm_ar_packed(x, pk, N, G, h))
+    rng = np.random.default_rng(3)
+    res = dev((rng.standard_normal((M, N)) * 4).astype(np.float16))
+    w = dev((1.0 + rng.uniform(-0.3, 0.3, size=N)).astype(np.float16))
+    r0, r1 = res.clone(), res.clone()
+    o0 = ops.w4gemm_ar_rmsnorm(x, qw, qz, sc, h, r0, w, 1e-6)
+    o1 = ops.w4gemm_ar_rmsnorm_packed(x, pk, N, G, h, r1, w, 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(o0, o1), mismatch(o1, o0)
+    assert torch.equal(r0, r1), mismatch(r1, r0)
+    assert ops.nvar_status(h, True) == 0
+    with pytest.raises(RuntimeError, match="needs"):
+        ops.w4gemm_ar_packed(x, pk[:-16], N, G, h)
+    with pytest.raises(RuntimeError, match="residual"):
+        ops.w4gemm_ar_rmsnorm_packed(x, pk, N, G, h, r1[:, :-32].contiguous(), w, 1e-6)
