@@ -6,10 +6,12 @@
  * This library provides, behind plain pointers and sizes:
  *   - an fp16 GEMM        y[M,N] = x[M,K] @ w[N,K]^T                      (b2_gemm_f16)
  *   - a W4A16 GEMM over GPTQ/Exllama-shuffled 4-bit weights                (b2_w4_gemm)
- *   - a one-shot all-reduce over NVLink peer memory                        (b2_nvar_*)
+ *   - an all-reduce over NVLink peer memory (one-shot, two-shot from 8 ranks) (b2_nvar_*)
  *   - the W4A16 GEMM with that all-reduce fused into its epilogue          (b2_w4_gemm_allreduce)
  *   - the same, followed in the same launch by the residual add + RMSNorm
  *     of the decoder layer                                        (b2_w4_gemm_allreduce_rmsnorm)
+ *   - a load-time repack of the W4 weights and the three W4 entry points above on it
+ *     (b2_w4_repack, b2_w4_gemm_packed, b2_w4_gemm_allreduce(_rmsnorm)_packed)
  * Every compute entry point launches on the caller's stream, never synchronises and never
  * allocates, so it can be captured in a CUDA graph.
  *
