@@ -16,6 +16,10 @@ CUDA events and taken as the max over ranks. The line also carries:
     kernels/check_w4.py:11-21; `x.float() @ w.float().T`, kernels/bench_skinny.py:44) timed on
     the host cores over a column sample of every GEMM of one layer and a row sample of the
     lm_head, scaled to a full step;
+  * `config4_with_norms`: the step with the decoder layer's residual add + RMSNorm after each
+    row-parallel layer, fused into its epilogue and as separate steps;
+  * `config4_packed_weights`: the step with every W4 weight repacked at load time (w4_repack,
+    then the *_packed operators), and whether its logits equal the plain step's bit for bit;
   * `extra` (N = 1): config 1 (fp16 lm_head GEMM) and config 0 (W4 4096 x 4096) on their own, as
     in the earlier default line.
 
