@@ -314,6 +314,10 @@ int b2_w4_gemm_allreduce_emulated(b2_nvar* const* handles, int ranks, const void
 #define B2_TUNE_NORM_NO_COOP 9    /* nonzero: launch the stream-K kernel's fused RMSNorm (its
                                      grid-wide barrier) without the cooperative attribute, so
                                      that residency rests on the grid size alone                */
+#define B2_TUNE_NORM_IN_LAUNCH 10  /* nonzero: the fused RMSNorm runs entirely inside the GEMM's
+                                     launch (the last cluster, or the stream-K grid after a
+                                     grid-wide barrier, finishes the rows) instead of in a short
+                                     finishing launch that follows it on the stream             */
 int b2_set_tuning(int key, int value);
 int b2_get_tuning(int key);
 

@@ -685,6 +685,102 @@ __device__ __forceinline__ bool norm_finish_cluster(const W4Args& p, const ArVie
   return ok;
 }
 
+// p.norm == 2 (the default): the fused launch stops after phase a. Each CTA adds its threads' row
+// sums (shuffle tree per warp, warps in order) into npart[blockIdx.x]; norm_finish_kernel, the
+// next launch on the stream, adds the grid's sums and finishes every element.
+__device__ __forceinline__ void norm_cta_sums(const W4Args& p, const float (&ss)[kMaxM],
+                                              float* s_norm) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+  for (int m = 0; m < kMaxM; ++m) {
+    float v = ss[m];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) s_norm[warp * kMaxM + m] = v;
+  }
+  named_bar_sync(1, kWarps * 32);
+  if (tid < kMaxM) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) v += s_norm[w * kMaxM + tid];
+    p.npart[(size_t)blockIdx.x * kMaxM + tid] = v;
+  }
+}
+
+// Phases b and c of the split RMSNorm, after a fused launch with p.norm == 2 (programmatic
+// dependent launch: nothing of that launch is read before grid_dep_wait). Every CTA adds the
+// `nparts` CTA sums of each row in the same fixed order (16 strided partial sums, then those in
+// order), so every CTA and every rank computes the same rstd bit for bit, then finishes its share
+// of the M x N elements in vectors V (uint4: 8 fp16, uint2: 4; N % 32 == 0, so a vector never
+// crosses a row): x = y + residual, residual <- fp16(x), y <- fp16(fp16(x * rstd) * weight).
+template <typename V>
+__global__ void __launch_bounds__(256) norm_finish_kernel(const __grid_constant__ W4Args p,
+                                                          int nparts) {
+  __shared__ float s_part[16 * kMaxM];
+  __shared__ float s_rstd[kMaxM];
+  grid_dep_launch();
+  grid_dep_wait();
+  constexpr int kH = (int)(sizeof(V) / 2);
+  const int tid = threadIdx.x;
+  const int per = p.M * p.N / kH, i0 = blockIdx.x * blockDim.x + tid;
+  // this thread's first vector is loaded before the row sums are added, to overlap the two
+  V y0 = {}, r0 = {}, w0 = {};
+  if (i0 < per) {
+    const int m = (i0 * kH) / p.N, n = i0 * kH - m * p.N;
+    const size_t o = (size_t)m * p.N + n;
+    y0 = __ldcg(reinterpret_cast<const V*>(p.y + o));
+    r0 = __ldcg(reinterpret_cast<const V*>(p.res + o));
+    w0 = __ldg(reinterpret_cast<const V*>(p.nw + n));
+  }
+  if (tid < 16 * kMaxM) {  // partial sum j of row m: CTAs j, j + 16, ... in order
+    const int m = tid & (kMaxM - 1), j = tid / kMaxM;
+    float v = 0.f;
+    for (int b0 = j; b0 < nparts; b0 += 16 * 16) {
+      float t[16];  // 16 independent loads in flight, then added in CTA order
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        const int b = b0 + 16 * u;
+        t[u] = b < nparts ? __ldcg(p.npart + (size_t)b * kMaxM + m) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 16; ++u) v += t[u];
+    }
+    s_part[j * kMaxM + m] = v;
+  }
+  __syncthreads();
+  if (tid < kMaxM) {
+    float v = 0.f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v += s_part[j * kMaxM + tid];
+    s_rstd[tid] = rsqrtf(v / (float)p.N + p.eps);
+  }
+  __syncthreads();
+  for (int i = i0; i < per; i += gridDim.x * blockDim.x) {
+    const int m = (i * kH) / p.N, n = i * kH - m * p.N;
+    const size_t o = (size_t)m * p.N + n;
+    V yv = y0, rv = r0, wv = w0;
+    if (i != i0) {
+      yv = __ldcg(reinterpret_cast<const V*>(p.y + o));
+      rv = __ldcg(reinterpret_cast<const V*>(p.res + o));
+      wv = __ldg(reinterpret_cast<const V*>(p.nw + n));
+    }
+    const __half* yh = reinterpret_cast<const __half*>(&yv);
+    __half* rh = reinterpret_cast<__half*>(&rv);
+    const __half* wh = reinterpret_cast<const __half*>(&wv);
+    V ov;
+    __half* oh = reinterpret_cast<__half*>(&ov);
+    const float rstd = s_rstd[m];
+#pragma unroll
+    for (int k = 0; k < kH; ++k) {
+      const float x = norm_x(yh[k], rh[k]);
+      rh[k] = __float2half_rn(x);
+      oh[k] = norm_out(x, rstd, wh[k]);
+    }
+    *reinterpret_cast<V*>(p.res + o) = rv;
+    *reinterpret_cast<V*>(p.y + o) = ov;
+  }
+}
+
 // A = (q - z) in fp16 (exact, see dequant_word) against B = x; the fp32 sum of each quantization
 // group is scaled once: acc += s * sum. Every weight is dequantized once per CTA and used for all
 // M rows.
@@ -990,7 +1086,8 @@ __device__ __forceinline__ void w4_body(const CUtensorMap& tm_qw, const CUtensor
       store_y(p, tile, colw, t, v);
       if (p.norm) norm_accum_lane(p, t, n, v, ss);
     }
-    if (p.norm) {
+    if (p.norm == 2) norm_cta_sums(p, ss, reinterpret_cast<float*>(smem + C::kNormOff));
+    if (p.norm == 1) {
       float* s_norm = reinterpret_cast<float*>(smem + C::kNormOff);
       if (!norm_rstd(p, ar, e, ss, s_norm, s_flag) && threadIdx.x == 0)
         atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
@@ -1444,7 +1541,8 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
       }
     }
     B2_TRC(6);
-    if (p.norm) {
+    if (p.norm == 2) norm_cta_sums(p, ss, reinterpret_cast<float*>(smem + C::kNormOff));
+    if (p.norm == 1) {
       float* s_norm = reinterpret_cast<float*>(smem + C::kNormOff);
       if (!norm_finish_cluster(p, ar, e, ss, s_norm, norm_bar, rstd_bar, s_flag, s_abort, crank,
                                CS, cid, NC) &&
@@ -1452,7 +1550,8 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
         atomicCAS(&ar_header(ar)->status, 0, B2_ERR_TIMEOUT);
     }
     named_bar_sync(1, kWarps * 32);
-    if (tid == 0 && !p.norm) ar_finish(ar, e);  // (norm launches advanced the generation above)
+    // (in-launch norm launches advanced the generation above)
+    if (tid == 0 && p.norm != 1) ar_finish(ar, e);
   }
   // Before this CTA exits, no peer may still write into its shared memory or arrive on its
   // barriers, and its own outgoing copies must be done reading its send buffer. On the normal
@@ -1470,7 +1569,7 @@ __device__ __forceinline__ void w4c_body(const CUtensorMap& tm_qw, const CUtenso
       *no_abort = 0;
       if (FUSED && !p.ll && !solo && crank == 0)
         mbar_wait_cluster(pub_bar, (uint32_t)((ntile - 1) & 1), no_abort);
-      if (FUSED && p.norm) {  // the leader's rstd here, and (leader) every CTA's row sums
+      if (FUSED && p.norm == 1) {  // the leader's rstd here, and (leader) every CTA's row sums
         *no_abort = 0;
         mbar_wait_cluster(rstd_bar, 0u, no_abort);
         *no_abort = 0;
@@ -1774,7 +1873,7 @@ int launch(const W4Args& a0, const void* qw, const void* qz, const void* sc, con
   // once. A cooperative launch gets that guarantee from the driver (or is refused), and it starts
   // only after the previous kernel: launched early, a grid's first CTAs take whatever slots the
   // previous grid leaves free and the rest may not fit beside them.
-  const bool barrier = FUSED && a.norm != 0;
+  const bool barrier = FUSED && a.norm == 1;
   return launch_kernel_ex(w4_kernel<GP, FUSED>, pl.sk.ctas, kThreads, C::kSmem, stream,
                           early && !barrier, barrier && !tuning(B2_TUNE_NORM_NO_COOP), m_qw, m_sc,
                           m_qz, m_x, a, view);
@@ -2136,6 +2235,38 @@ int fused_args(b2_nvar* h, const void* a, const void* qw, const void* qz, const 
   return B2_OK;
 }
 
+// The finishing launch of the split RMSNorm (norm_finish_kernel) after a fused launch of
+// `nparts` CTAs. 128 threads per CTA, one vector per thread.
+int launch_norm_finish(const W4Args& a, int nparts, cudaStream_t stream) {
+  const int kH = a.norm_v16 ? 8 : 4;
+  const int per = a.M * a.N / kH;
+  const int grid = std::max(1, std::min((per + 127) / 128, kWsMaxCtas));
+  if (a.norm_v16)
+    return launch_kernel(norm_finish_kernel<uint4>, grid, 128, 0, stream, /*early=*/true, a,
+                         nparts);
+  return launch_kernel(norm_finish_kernel<uint2>, grid, 128, 0, stream, /*early=*/true, a, nparts);
+}
+
+// One rank's fused launch. With the RMSNorm the default is the split form (p.norm = 2): the
+// fused launch stores the all-reduced rows and its CTAs' row sums, and norm_finish_kernel follows
+// on the stream; B2_TUNE_NORM_IN_LAUNCH keeps all of it in the one launch (p.norm = 1).
+// Early launch is safe here too: the generation is read after griddepcontrol.wait, and a
+// dependent grid starts only once every CTA of this one is resident, so none of the CTAs that
+// wait for peers in the second phase can be held back. (The cluster kernel's in-launch RMSNorm
+// needs no co-residency either: its last cluster finishes the rows. The stream-K kernel's, with a
+// grid-wide barrier, is launched without early start; see launch.)
+int launch_fused(W4Args& args, const void* qw, const void* qz, const void* sc, const ArView& v,
+                 cudaStream_t stream) {
+  if (args.norm && tuning(B2_TUNE_NORM_IN_LAUNCH) == 0) args.norm = 2;
+  if (args.norm != 2) return dispatch<true>(args, qw, qz, sc, &v, stream, /*early=*/true);
+  Plan pl;
+  int rc = plan_for<true>(args, kWsMaxCtas, &pl);
+  if (rc) return rc;
+  rc = launch_plan<true>(args, qw, qz, sc, &v, pl, /*early=*/true, stream);
+  if (rc) return rc;
+  return launch_norm_finish(args, pl.cs > 0 ? pl.cs * pl.nc : pl.sk.ctas, stream);
+}
+
 int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* qz, const void* sc,
                         void* y, int M, int K, int N, int G, void* ws, size_t ws_bytes,
                         cudaStream_t stream, void* residual = nullptr, const void* nw = nullptr,
@@ -2145,12 +2276,7 @@ int launch_w4_allreduce(b2_nvar* h, const void* a, const void* qw, const void* q
   const int rc = fused_args(h, a, qw, qz, sc, y, M, K, N, G, ws, ws_bytes, residual, nw, eps,
                             &args, &v);
   if (rc) return rc;
-  // Early launch is safe here too: the generation is read after griddepcontrol.wait, and a
-  // dependent grid starts only once every CTA of this one is resident, so none of the CTAs that
-  // wait for peers in the second phase can be held back. (The cluster kernel's RMSNorm needs no
-  // co-residency either: its last cluster finishes the rows. The stream-K kernel's, with a
-  // grid-wide barrier, is launched without early start; see launch.)
-  return dispatch<true>(args, qw, qz, sc, &v, stream, /*early=*/true);
+  return launch_fused(args, qw, qz, sc, v, stream);
 }
 
 // The fused launch on weights repacked by w4_repack (`packed` in place of qw, qz, sc).
@@ -2164,7 +2290,7 @@ int launch_w4_allreduce_packed(b2_nvar* h, const void* a, const void* packed, vo
   if (rc) return rc;
   args.pk = static_cast<const uint8_t*>(packed);
   args.pk_unit = packed_unit_bytes(G);
-  return dispatch<true>(args, nullptr, nullptr, nullptr, &v, stream, /*early=*/true);
+  return launch_fused(args, nullptr, nullptr, nullptr, v, stream);
 }
 
 // `R` ranks of one group in one cooperative launch on this GPU (grid.y = rank). Every rank gets
