@@ -849,7 +849,8 @@ def run_profile(args):
 
 def run_norm_epilogue(args):
     """Row-parallel W4 layer + residual add + RMSNorm on one GPU (one-rank all-reduce handle):
-    the fused launch (w4gemm_ar_rmsnorm) against the fused GEMM + all-reduce followed by a
+    the fused call (w4gemm_ar_rmsnorm: the GEMM + all-reduce launch, then its finishing launch;
+    and with the norm inside the GEMM's launch) against the fused GEMM + all-reduce followed by a
     separate norm - vLLM's own CUDA kernel (torch.ops._C.fused_add_rms_norm) when vLLM loads, and
     the torch restatement of its reference code (vllm/ir/ops/layernorm.py:48-58). Per-rank
     shards of o_proj and down_proj at TP 1..8, M=8; graph replay over weight copies that exceed
@@ -904,8 +905,9 @@ def run_norm_epilogue(args):
                 # the same launch without early start, as the norm epilogue is launched
                 "gemm_ar_no_early_launch": lambda t: ops.w4gemm_ar(x, *t, h),
                 "gemm_ar_norm_fused": lambda t: ops.w4gemm_ar_rmsnorm(x, *t, h, r, w, eps),
-                # the same without the cooperative launch attribute (B2_TUNE_NORM_NO_COOP)
-                "gemm_ar_norm_fused_no_coop": lambda t: ops.w4gemm_ar_rmsnorm(x, *t, h, r, w, eps),
+                # the norm inside the GEMM's launch instead of a finishing launch
+                # (B2_TUNE_NORM_IN_LAUNCH)
+                "gemm_ar_norm_in_launch": lambda t: ops.w4gemm_ar_rmsnorm(x, *t, h, r, w, eps),
                 "gemm_ar_then_torch_norm": lambda t: torch_norm(ops.w4gemm_ar(x, *t, h), r),
             }
             if vllm_norm is not None:
@@ -920,7 +922,7 @@ def run_norm_epilogue(args):
                 reps = max(copies, min(64, 20 * copies)) // copies * copies
                 capi.check(lib.b2_set_tuning(3, 1 if vname == "gemm_ar_no_early_launch" else 0),
                            "b2_set_tuning")  # B2_TUNE_NO_PDL, read at launch (and capture) time
-                capi.check(lib.b2_set_tuning(9, 1 if vname == "gemm_ar_norm_fused_no_coop" else 0),
+                capi.check(lib.b2_set_tuning(10, 1 if vname == "gemm_ar_norm_in_launch" else 0),
                            "b2_set_tuning")
                 try:
                     for t in ws:

@@ -226,7 +226,7 @@ int b2_nvar_allreduce(b2_nvar* ar, const void* in, void* out, size_t count, int 
 int b2_w4_gemm_allreduce(b2_nvar* ar, const void* a, const void* qw, const void* qz,
                          const void* sc, void* y, int M, int K, int N, int group_size, void* ws,
                          size_t ws_bytes, void* stream);
-/* The same layer followed, in the same launch, by the residual add + RMSNorm that the decoder
+/* The same layer followed, in the same call, by the residual add + RMSNorm that the decoder
  * layer runs on the all-reduced output (vLLM's fused_add_rms_norm, vllm/ir/ops/layernorm.py:40-60
  * in vLLM 0.22; no counterpart in the reference's library):
  *   s        = allreduce_over_ranks(a_rank @ dequant(qw_rank, ...))     as b2_w4_gemm_allreduce
@@ -235,11 +235,12 @@ int b2_w4_gemm_allreduce(b2_nvar* ar, const void* a, const void* qw, const void*
  *   y        = fp16(fp16(x * rsqrt(sum_n(x^2) / N + eps)) * norm_weight[n])
  * residual : [M, N] fp16, read and written; norm_weight : [N] fp16; both 8-byte aligned, and
  * y, residual and norm_weight must not overlap. 0 <= eps <= 1. The row sums are added in a fixed
- * order, so y and residual are bit-identical on every rank and from call to call. One
- * grid-wide barrier inside the kernel (bounded by the handle's timeout; B2_ERR_TIMEOUT in the
- * handle's status if it gives up). The barrier needs all of the launch's CTAs resident at once,
- * so this launch never starts early (no programmatic dependent launch), and kernels that other
- * streams keep running on the GPU for its whole duration can make it time out. */
+ * order, so y and residual are bit-identical on every rank and from call to call. Two launches on
+ * `stream`: the fused GEMM + all-reduce, which also stores its CTAs' row sums of squares, then a
+ * short kernel that adds them and writes residual and y (both may start early, as programmatic
+ * dependent launches). B2_TUNE_NORM_IN_LAUNCH keeps it to one launch: the GEMM's last cluster
+ * finishes the rows, or, in the stream-K kernel, one grid-wide barrier (bounded by the handle's
+ * timeout; B2_ERR_TIMEOUT in the handle's status if it gives up) in a cooperative launch. */
 int b2_w4_gemm_allreduce_rmsnorm(b2_nvar* ar, const void* a, const void* qw, const void* qz,
                                  const void* sc, void* residual, const void* norm_weight,
                                  float eps, void* y, int M, int K, int N, int group_size,

@@ -330,7 +330,7 @@ at::Tensor w4gemm_ar(const at::Tensor& a, const at::Tensor& qw, const at::Tensor
   return y;
 }
 
-// w4gemm_ar followed, in the same launch, by vLLM's fused residual add + RMSNorm
+// w4gemm_ar followed, in the same call, by vLLM's fused residual add + RMSNorm
 // (b2_w4_gemm_allreduce_rmsnorm): `residual` becomes residual + all-reduced rows, in place, and
 // the normalised rows are returned.
 at::Tensor w4gemm_ar_rmsnorm(const at::Tensor& a, const at::Tensor& qw, const at::Tensor& qz,

@@ -131,7 +131,7 @@ class NvlinkAllReduce:
 
     def w4_gemm_all_reduce_rmsnorm(self, x, w_q, w_zp, w_s, residual, weight,
                                    eps: float) -> torch.Tensor:
-        """The same layer followed, in the same launch, by the decoder layer's residual add +
+        """The same layer followed, in the same call, by the decoder layer's residual add +
         RMSNorm (vLLM's fused_add_rms_norm): ``residual`` is updated in place, the normalised
         rows are returned."""
         return self.ops.w4gemm_ar_rmsnorm(x, w_q, w_zp, w_s, self.handle, residual, weight, eps)
