@@ -33,6 +33,9 @@ B2_TUNE_W4_PATH = 4
 B2_TUNE_W4_CLUSTER = 5
 B2_TUNE_AR_FLAGS = 6
 B2_TUNE_AR_TWO_SHOT = 7
+B2_TUNE_W4_NO_ALIAS = 8
+B2_TUNE_NORM_NO_COOP = 9
+B2_TUNE_NORM_IN_LAUNCH = 10
 
 _vp, _i, _sz, _u64 = C.c_void_p, C.c_int, C.c_size_t, C.c_uint64
 _SIGS = {

@@ -6,6 +6,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+from pathlib import Path
 
 import pytest
 
@@ -137,6 +138,21 @@ def test_tuning_knobs(capi):
     assert lib.b2_get_tuning(capi.B2_TUNE_CTAS_PER_SM) == 2
     assert lib.b2_set_tuning(capi.B2_TUNE_CTAS_PER_SM, 0) == 0
     assert lib.b2_set_tuning(99, 1) == capi.B2_ERR_INVALID_ARG
+
+
+def test_tuning_keys_match_header(capi):
+    """Every B2_TUNE_* key of include/b2_skinny.h has the same value in the Python bindings, and
+    the library accepts it."""
+    import re
+
+    header = (Path(__file__).resolve().parent.parent / "include" / "b2_skinny.h").read_text()
+    keys = dict(re.findall(r"#define (B2_TUNE_\w+) (\d+)", header))
+    assert len(keys) >= 10
+    lib = capi.lib()
+    for name, value in keys.items():
+        assert getattr(capi, name) == int(value), name
+        saved = lib.b2_get_tuning(int(value))
+        assert lib.b2_set_tuning(int(value), saved) == 0, name
 
 
 def test_registry_put_get_unlink(capi):
